@@ -1,0 +1,546 @@
+// The dense multiply of CAIRN's tensor runtime, rebuilt for sm_100a.
+//
+// What it computes (the mma_unordered contract, runtime/cairn_tensor.hpp:1-6 and docs/numerics.md "The tensor-core
+// multiply"): C (m x n, f32) += A (m x k) * B (k x n) over one storage float, each product exact in f32 and each
+// output the f32 sum of its old value and its k products in an order the hardware picks. Beside it, the same product
+// with either operand transposed (the backward of a dense layer: dX = dY * W^T, dW = X^T * dY) and with a fused
+// epilogue (C = act(A * B + bias) cast to bf16, or C = A * B stored as f32).
+//
+// How (one persistent CTA per SM, 192 threads, 6 warps):
+//   warp 0, one lane   TMA producer: for each output tile and each 128-byte slice of k, loads the A tile (128 rows)
+//                      and the B tile (BN columns) into a ring of shared-memory stages, 128-byte swizzled, and
+//                      arms the stage's "full" mbarrier with the byte count.
+//   warp 1             allocates the tile accumulators in tensor memory (2 x BN columns of 128 lanes, double
+//                      buffered); one lane issues tcgen05.mma (M=128, N=BN, 32 bytes of k per instruction) from
+//                      the stage's shared-memory descriptors, commits each stage back to its "empty" mbarrier, and
+//                      commits each finished accumulator to its "tmem full" mbarrier.
+//   warps 2-5          epilogue: each warp owns 32 TMEM lanes (rows); it drains the accumulator 32 columns at a time
+//                      with tcgen05.ld, frees the accumulator for the next tile, and writes the tile to global
+//                      memory with the requested epilogue (C += acc, C = acc, or bf16(act(acc + bias))).
+// Tiles are visited in groups of 8 column blocks so a wave of 148 CTAs shares A rows and B columns in L2.
+//
+// Operands are read straight from the caller's row-major arrays through TMA tensor maps; TMA zero-fills past the
+// edges, so any m, n, k works as long as the rows start on 16 bytes (the tensor-map rule). Shapes that break it, and
+// k == 0, run the SIMT tile kernel at the end of this file, which computes the same products.
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include "gemm.h"
+#include "ptx.cuh"
+
+namespace cb {
+
+// ---------------------------------------------------------------------------------------------------------------
+// Formats
+// ---------------------------------------------------------------------------------------------------------------
+template <int FMT> struct Fmt;
+template <> struct Fmt<FMT_BF16> { static constexpr int bytes = 2, kind = KIND_F16, code = 1; };
+template <> struct Fmt<FMT_F16> { static constexpr int bytes = 2, kind = KIND_F16, code = 0; };
+template <> struct Fmt<FMT_E4M3> { static constexpr int bytes = 1, kind = KIND_F8F6F4, code = 0; };
+template <> struct Fmt<FMT_E5M2> { static constexpr int bytes = 1, kind = KIND_F8F6F4, code = 1; };
+template <> struct Fmt<FMT_TF32> { static constexpr int bytes = 4, kind = KIND_TF32, code = 2; };
+
+struct TcParams {
+  int m, n, k;
+  int a_mn;       // A is stored k x m (the transposed operand): M-major in shared memory
+  int b_k;        // B is stored n x k (the transposed operand): K-major in shared memory
+  int out_kind;   // OUT_ACC_F32, OUT_STORE_F32 or OUT_BF16
+  void* out;
+  const float* bias;
+  int act;
+  int vec;        // every output row starts on 16 bytes and holds whole 16-byte groups
+  std::uint32_t* fault;
+};
+
+constexpr int BM = 128;              // rows of a tile: the MMA's M, one TMEM lane per row
+constexpr int SLICE = 128;           // bytes of k per stage: one 128-byte swizzle row
+constexpr int A_STAGE = BM * SLICE;  // 16 KiB
+constexpr int GROUP_N = 8;           // column blocks per rasterization group
+
+template <int BN> struct Shape {
+  static constexpr int B_STAGE = BN * SLICE;
+  static constexpr int STAGES = (200 * 1024) / (A_STAGE + B_STAGE);
+  static constexpr int TMEM_COLS = 2 * BN;  // two accumulators
+  static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_STAGE) + 256;
+  static_assert(TMEM_COLS == 256 || TMEM_COLS == 512, "TMEM allocations are powers of two");
+};
+
+__device__ __forceinline__ void tile_of(int t, int num_m, int num_n, int& mb, int& nb) {
+  const int per_group = num_m * GROUP_N;
+  const int g = t / per_group;
+  const int first = g * GROUP_N;
+  const int width = min(GROUP_N, num_n - first);
+  const int r = t - g * per_group;
+  mb = r / width;
+  nb = first + r % width;
+}
+
+// Waits out copies or MMAs still in flight on the exit path, ignoring the abort flag but still bounded.
+__device__ __noinline__ void drain_wait(std::uint64_t* bar, std::uint32_t parity, std::uint32_t* fault) {
+  const std::uint64_t start = globaltimer();
+  while (!mbar_test(bar, parity)) {
+    if (globaltimer() - start > WAIT_LIMIT_NS) {
+      atomicOr(fault, static_cast<std::uint32_t>(FAULT_DRAIN));
+      return;
+    }
+  }
+}
+
+template <int FMT>
+__device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col, const std::uint32_t (&r)[32]) {
+  if (row >= p.m) return;
+  if (p.out_kind == OUT_BF16) {
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float b = (p.bias != nullptr && col + j < p.n) ? __ldg(p.bias + col + j) : 0.0f;
+      float x = __fadd_rn(__uint_as_float(r[j]), b);
+      if (p.act == ACT_RELU) x = x < 0.0f ? 0.0f : x;
+      v[j] = x;
+    }
+    __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + static_cast<std::size_t>(row) * p.n + col;
+    if (p.vec && col + 32 <= p.n) {
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
+        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
+        __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
+        std::memcpy(&w.x, &h0, 4);
+        std::memcpy(&w.y, &h1, 4);
+        std::memcpy(&w.z, &h2, 4);
+        std::memcpy(&w.w, &h3, 4);
+        d4[q] = w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col + j < p.n) dst[j] = __float2bfloat16_rn(v[j]);
+    }
+  } else {
+    float* dst = static_cast<float*>(p.out) + static_cast<std::size_t>(row) * p.n + col;
+    const bool acc = p.out_kind == OUT_ACC_F32;
+    if (p.vec && col + 32 <= p.n) {
+      float4* d4 = reinterpret_cast<float4*>(dst);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        float4 o = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]), __uint_as_float(r[4 * q + 2]),
+                               __uint_as_float(r[4 * q + 3]));
+        if (acc) {
+          const float4 old = d4[q];
+          o.x = __fadd_rn(old.x, o.x);
+          o.y = __fadd_rn(old.y, o.y);
+          o.z = __fadd_rn(old.z, o.z);
+          o.w = __fadd_rn(old.w, o.w);
+        }
+        d4[q] = o;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col + j < p.n) dst[j] = acc ? __fadd_rn(dst[j], __uint_as_float(r[j])) : __uint_as_float(r[j]);
+    }
+  }
+}
+
+template <int FMT, int BN>
+__global__ void __launch_bounds__(192, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                   const TcParams p) {
+  using F = Fmt<FMT>;
+  using S = Shape<BN>;
+  constexpr int STAGES = S::STAGES;
+  constexpr int CH = SLICE / F::bytes;              // elements per 128-byte row: the k of a stage, the width of a chunk
+  constexpr int MMA_K_BYTES = 32;                   // every kind consumes 32 bytes of k per instruction
+  constexpr int MMA_K_ROWS = MMA_K_BYTES / F::bytes;  // ... which is this many k rows of an M/N-major tile
+  constexpr std::uint32_t STAGE_BYTES = A_STAGE + S::B_STAGE;
+
+  extern __shared__ std::uint8_t smem_raw[];
+  std::uint8_t* base = reinterpret_cast<std::uint8_t*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) &
+                                                       ~static_cast<std::uintptr_t>(1023));
+  std::uint8_t* a_smem = base;
+  std::uint8_t* b_smem = base + STAGES * A_STAGE;
+  std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(b_smem + STAGES * S::B_STAGE);
+  std::uint64_t* full = bars;
+  std::uint64_t* empty = bars + STAGES;
+  std::uint64_t* tfull = bars + 2 * STAGES;
+  std::uint64_t* tempty = tfull + 2;
+  std::uint64_t* drain = tempty + 2;
+  std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(drain + 1);
+  volatile std::uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int num_m = (p.m + BM - 1) / BM, num_n = (p.n + BN - 1) / BN;
+  const int tiles = num_m * num_n;
+  const int num_kb = (p.k + CH - 1) / CH;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const std::uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_b);
+      std::uint32_t stage = 0, phase = 0;
+      std::uint32_t issued = 0, parity_of = 0;  // per stage: ever loaded, and the parity of its last load
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+        int mb, nb;
+        tile_of(t, num_m, num_n, mb, nb);
+        const int m0 = mb * BM, n0 = nb * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.fault, FAULT_WAIT_EMPTY)) goto producer_done;
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          issued |= 1u << stage;
+          parity_of = (parity_of & ~(1u << stage)) | (phase << stage);
+          const std::uint32_t a_dst = smem_u32(a_smem + stage * A_STAGE);
+          const std::uint32_t b_dst = smem_u32(b_smem + stage * S::B_STAGE);
+          const int k0 = kb * CH;
+          if (!p.a_mn) {
+            tma_load_2d(a_dst, &tm_a, &full[stage], k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / CH; ++c) tma_load_2d(a_dst + c * CH * SLICE, &tm_a, &full[stage], m0 + c * CH, k0);
+          }
+          if (p.b_k) {
+            tma_load_2d(b_dst, &tm_b, &full[stage], k0, n0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / CH; ++c) tma_load_2d(b_dst + c * CH * SLICE, &tm_b, &full[stage], n0 + c * CH, k0);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:
+      if (*abort_flag) {
+        for (int s = 0; s < STAGES; ++s)
+          if (issued & (1u << s)) drain_wait(&full[s], (parity_of >> s) & 1u, p.fault);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const std::uint32_t idesc =
+          idesc_make(F::code, F::code, p.a_mn != 0, p.b_k == 0, static_cast<std::uint32_t>(BM), BN);
+      // Leading/stride byte offsets: a K-major tile is rows of 128 bytes, 8-row swizzle atoms 1024 bytes apart; an
+      // M/N-major tile is CH-element chunks of SLICE rows each (chunk stride CH * SLICE bytes), 8 k rows per atom.
+      const std::uint32_t a_lbo = p.a_mn ? CH * SLICE : 16u, b_lbo = p.b_k ? 16u : CH * SLICE;
+      std::uint32_t stage = 0, phase = 0, it = 0;
+      for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+        const std::uint32_t acc = it & 1u, acc_phase = (it >> 1) & 1u;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.fault, FAULT_WAIT_TEMPTY)) goto mma_done;
+        tc_fence_after();
+        const std::uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.fault, FAULT_WAIT_FULL)) goto mma_done;
+          tc_fence_after();
+          const std::uint32_t a_addr = smem_u32(a_smem + stage * A_STAGE);
+          const std::uint32_t b_addr = smem_u32(b_smem + stage * S::B_STAGE);
+#pragma unroll
+          for (int kk = 0; kk < SLICE / MMA_K_BYTES; ++kk) {
+            const std::uint32_t a_off = p.a_mn ? kk * (MMA_K_ROWS / 8) * 1024 : kk * MMA_K_BYTES;
+            const std::uint32_t b_off = p.b_k ? kk * MMA_K_BYTES : kk * (MMA_K_ROWS / 8) * 1024;
+            const std::uint64_t a_desc = sdesc_sw128(a_addr + a_off, a_lbo, 1024);
+            const std::uint64_t b_desc = sdesc_sw128(b_addr + b_off, b_lbo, 1024);
+            umma<F::kind>(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        tc_commit(&tfull[acc]);
+      }
+    mma_done:
+      // Every MMA this thread issued completes before the accumulators are released.
+      tc_commit(drain);
+      drain_wait(drain, 0u, p.fault);
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;  // TMEM lanes a warp may read: 32 * (warp id % 4) .. + 31
+    std::uint32_t it = 0;
+    for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
+      const std::uint32_t acc = it & 1u, acc_phase = (it >> 1) & 1u;
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.fault, FAULT_WAIT_TFULL)) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_of(t, num_m, num_n, mb, nb);
+      const int row = mb * BM + quarter * 32 + lane;
+      const std::uint32_t t_row = tmem_base + (static_cast<std::uint32_t>(quarter * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        std::uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c, r);
+        tmem_wait_ld();
+        if (c + 32 == BN) {  // the whole accumulator is in registers: hand it back to the MMA issuer
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&tempty[acc]);
+        }
+        store_chunk<FMT>(p, row, nb * BN + c, r);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// The SIMT tile kernel: shapes the tensor maps cannot describe (a row not on 16 bytes), and k == 0. 64 x 64 tiles,
+// 256 threads of 4 x 4 outputs, k in steps of 16 staged through shared memory as f32 (every storage float widens to
+// f32 exactly; tf32 operands are used at full f32 precision here).
+// ---------------------------------------------------------------------------------------------------------------
+template <int FMT> __device__ __forceinline__ float widen(const void* base, std::size_t i);
+template <> __device__ __forceinline__ float widen<FMT_BF16>(const void* b, std::size_t i) {
+  return __uint_as_float(static_cast<std::uint32_t>(static_cast<const std::uint16_t*>(b)[i]) << 16);
+}
+template <> __device__ __forceinline__ float widen<FMT_F16>(const void* b, std::size_t i) {
+  return __half2float(__ushort_as_half(static_cast<const std::uint16_t*>(b)[i]));
+}
+__device__ __forceinline__ float widen_small(std::uint32_t bits, int E, int M, bool has_inf) {
+  const std::uint32_t sign = (bits >> (E + M)) & 1u, e = (bits >> M) & ((1u << E) - 1u), f = bits & ((1u << M) - 1u);
+  const std::uint32_t top = (1u << E) - 1u;
+  const int bias = (1 << (E - 1)) - 1;
+  float v;
+  if (e == top && (has_inf || f == (1u << M) - 1u)) v = (has_inf && f == 0) ? __int_as_float(0x7f800000) : __int_as_float(0x7fc00000);
+  else if (e == 0) v = scalbnf(static_cast<float>(f), 1 - bias - M);
+  else v = scalbnf(static_cast<float>((1u << M) | f), static_cast<int>(e) - bias - M);
+  return sign ? -v : v;
+}
+template <> __device__ __forceinline__ float widen<FMT_E4M3>(const void* b, std::size_t i) {
+  return widen_small(static_cast<const std::uint8_t*>(b)[i], 4, 3, false);
+}
+template <> __device__ __forceinline__ float widen<FMT_E5M2>(const void* b, std::size_t i) {
+  return widen_small(static_cast<const std::uint8_t*>(b)[i], 5, 2, true);
+}
+template <> __device__ __forceinline__ float widen<FMT_TF32>(const void* b, std::size_t i) {
+  return static_cast<const float*>(b)[i];
+}
+
+template <int FMT>
+__global__ void __launch_bounds__(256) simt_gemm_kernel(const void* a, const void* b, const TcParams p) {
+  __shared__ float as[16][64 + 1];
+  __shared__ float bs[16][64 + 1];
+  const int tiles_n = (p.n + 63) / 64;
+  const int tiles = ((p.m + 63) / 64) * tiles_n;
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  for (int t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int m0 = (t / tiles_n) * 64, n0 = (t % tiles_n) * 64;
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    for (int k0 = 0; k0 < p.k; k0 += 16) {
+      for (int e = threadIdx.x; e < 64 * 16; e += 256) {
+        const int i = e / 16, q = e % 16;  // A(i, q)
+        const int r = m0 + i, kk = k0 + q;
+        as[q][i] = (r < p.m && kk < p.k)
+                       ? widen<FMT>(a, p.a_mn ? static_cast<std::size_t>(kk) * p.m + r
+                                              : static_cast<std::size_t>(r) * p.k + kk)
+                       : 0.0f;
+        const int j = e % 64, q2 = e / 64;  // B(q2, j)
+        const int cidx = n0 + j, kk2 = k0 + q2;
+        bs[q2][j] = (cidx < p.n && kk2 < p.k)
+                        ? widen<FMT>(b, p.b_k ? static_cast<std::size_t>(cidx) * p.k + kk2
+                                              : static_cast<std::size_t>(kk2) * p.n + cidx)
+                        : 0.0f;
+      }
+      __syncthreads();
+#pragma unroll
+      for (int q = 0; q < 16; ++q) {
+        float x[4], y[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x[i] = as[q][ty * 4 + i];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) y[j] = bs[q][tx * 4 + j];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = __fadd_rn(acc[i][j], __fmul_rn(x[i], y[j]));
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int row = m0 + ty * 4 + i;
+      if (row >= p.m) continue;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int col = n0 + tx * 4 + j;
+        if (col >= p.n) continue;
+        const std::size_t o = static_cast<std::size_t>(row) * p.n + col;
+        if (p.out_kind == OUT_BF16) {
+          float v = __fadd_rn(acc[i][j], p.bias ? p.bias[col] : 0.0f);
+          if (p.act == ACT_RELU) v = v < 0.0f ? 0.0f : v;
+          static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
+        } else if (p.out_kind == OUT_ACC_F32) {
+          float* c = static_cast<float*>(p.out);
+          c[o] = __fadd_rn(c[o], acc[i][j]);
+        } else {
+          static_cast<float*>(p.out)[o] = acc[i][j];
+        }
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------------------------------------------
+namespace {
+
+using EncodeTiled = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                 const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encoder() {
+  static EncodeTiled fn = []() -> EncodeTiled {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return nullptr;
+    return reinterpret_cast<EncodeTiled>(f);
+  }();
+  return fn;
+}
+
+CUtensorMapDataType map_type(int fmt) {
+  switch (fmt) {
+    case FMT_BF16: return CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+    case FMT_F16: return CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    case FMT_TF32: return CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    default: return CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  }
+}
+
+// A 2-D row-major array of `rows` rows of `cols` elements, read in boxes of box_cols x box_rows, 128-byte swizzled.
+bool encode(CUtensorMap* map, int fmt, const void* base, std::uint64_t cols, std::uint64_t rows, int esize,
+            std::uint32_t box_cols, std::uint32_t box_rows) {
+  EncodeTiled fn = encoder();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * static_cast<cuuint64_t>(esize)};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, map_type(fmt), 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+int esize_of(int fmt) { return fmt == FMT_TF32 ? 4 : (fmt == FMT_E4M3 || fmt == FMT_E5M2) ? 1 : 2; }
+
+bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
+
+template <int FMT, int BN>
+cudaError_t launch_tc(const GemmArgs& g, const TcParams& p, cudaStream_t stream, int sms) {
+  using S = Shape<BN>;
+  constexpr int CH = SLICE / Fmt<FMT>::bytes;
+  const int es = Fmt<FMT>::bytes;
+  CUtensorMap ta, tb;
+  const bool ok_a = g.trans_a ? encode(&ta, FMT, g.a, g.m, g.k, es, CH, CH) : encode(&ta, FMT, g.a, g.k, g.m, es, CH, BM);
+  const bool ok_b = g.trans_b ? encode(&tb, FMT, g.b, g.k, g.n, es, CH, BN) : encode(&tb, FMT, g.b, g.n, g.k, es, CH, CH);
+  if (!ok_a || !ok_b) return cudaErrorInvalidValue;
+  // The shared-memory opt-in is a property of the kernel on each device: set once per device before its first launch.
+  static std::atomic<std::uint64_t> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const std::uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(tc_gemm_kernel<FMT, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const int tiles = ((p.m + BM - 1) / BM) * ((p.n + BN - 1) / BN);
+  const int grid = tiles < sms ? tiles : sms;
+  tc_gemm_kernel<FMT, BN><<<grid, 192, S::SMEM, stream>>>(ta, tb, p);
+  return cudaGetLastError();
+}
+
+template <int FMT> cudaError_t launch_simt(const GemmArgs& g, const TcParams& p, cudaStream_t stream, int sms) {
+  const int tiles = ((p.m + 63) / 64) * ((p.n + 63) / 64);
+  const int grid = tiles < sms * 8 ? tiles : sms * 8;
+  simt_gemm_kernel<FMT><<<grid, 256, 0, stream>>>(g.a, g.b, p);
+  return cudaGetLastError();
+}
+
+template <int FMT> cudaError_t dispatch(const GemmArgs& g, const TcParams& p, cudaStream_t s, int sms, bool tc) {
+  if (!tc) return launch_simt<FMT>(g, p, s, sms);
+  if (p.n > 128) return launch_tc<FMT, 256>(g, p, s, sms);
+  return launch_tc<FMT, 128>(g, p, s, sms);
+}
+
+}  // namespace
+
+// Whether the tensor-core path can read the operands through TMA: 16-byte aligned bases and row strides, extents
+// that fit the tensor map, and at least one slice of k.
+bool tensor_path_ok(const GemmArgs& g) {
+  const std::uint64_t es = static_cast<std::uint64_t>(esize_of(g.fmt));
+  if (g.k == 0 || g.m == 0 || g.n == 0) return false;
+  if (!aligned16(g.a) || !aligned16(g.b)) return false;
+  const std::uint64_t a_row = (g.trans_a ? g.m : g.k) * es, b_row = (g.trans_b ? g.k : g.n) * es;
+  if (a_row % 16 || b_row % 16) return false;
+  const std::uint64_t lim = 1ull << 31;
+  return g.m < lim && g.n < lim && g.k < lim;
+}
+
+cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream, int sms, std::uint32_t* fault) {
+  TcParams p{};
+  p.m = static_cast<int>(g.m);
+  p.n = static_cast<int>(g.n);
+  p.k = static_cast<int>(g.k);
+  p.a_mn = g.trans_a;
+  p.b_k = g.trans_b;
+  p.out_kind = g.out_kind;
+  p.out = g.out;
+  p.bias = g.bias;
+  p.act = g.act;
+  p.fault = fault;
+  const std::uint64_t out_es = g.out_kind == OUT_BF16 ? 2 : 4;
+  p.vec = aligned16(g.out) && (g.n * out_es) % 16 == 0;
+  const bool tc = tensor_path_ok(g);
+  switch (g.fmt) {
+    case FMT_BF16: return dispatch<FMT_BF16>(g, p, stream, sms, tc);
+    case FMT_F16: return dispatch<FMT_F16>(g, p, stream, sms, tc);
+    case FMT_E4M3: return dispatch<FMT_E4M3>(g, p, stream, sms, tc);
+    case FMT_E5M2: return dispatch<FMT_E5M2>(g, p, stream, sms, tc);
+    case FMT_TF32: return dispatch<FMT_TF32>(g, p, stream, sms, tc);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace cb

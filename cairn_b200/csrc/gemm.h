@@ -1,0 +1,44 @@
+// Internal interface between the C ABI (abi.cu) and the kernels (gemm.cu, stream.cu).
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace cb {
+
+// The same values as enum cairn_b200_format / cairn_b200_out / cairn_b200_act in include/cairn_b200.h.
+enum : int { FMT_BF16 = 0, FMT_F16 = 1, FMT_E4M3 = 2, FMT_E5M2 = 3, FMT_TF32 = 4 };
+enum : int { OUT_ACC_F32 = 0, OUT_STORE_F32 = 1, OUT_BF16 = 2 };
+enum : int { ACT_NONE = 0, ACT_RELU = 1 };
+
+struct GemmArgs {
+  int fmt;
+  std::uint64_t m, n, k;
+  const void* a;
+  int trans_a;
+  const void* b;
+  int trans_b;
+  void* out;
+  int out_kind;
+  const float* bias;
+  int act;
+};
+
+// True when the tensor-core path reads both operands through TMA (otherwise the SIMT tile kernel runs).
+bool tensor_path_ok(const GemmArgs& g);
+// Queues the product on `stream`; `sms` is the device's SM count, `fault` its fault word.
+cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream, int sms, std::uint32_t* fault);
+
+// Streaming kernels (stream.cu). Scratch: `partials` holds one 16-byte cell per block of the grid, `ticket` one
+// counter that must be zero before the launch and is zero again after it.
+constexpr int STREAM_THREADS = 512;
+int stream_grid(int sms);  // blocks a streaming launch uses
+std::size_t reduce_scratch_bytes(int sms);
+cudaError_t saxpy_f32_launch(std::size_t n, float* out, const float* x, const float* y, float a, cudaStream_t s,
+                             int sms);
+cudaError_t sum_f32_launch(std::size_t n, const float* x, float* out_f32, double* out_f64, void* scratch,
+                           cudaStream_t s, int sms);
+cudaError_t sum_u64_launch(std::size_t n, const std::uint64_t* x, std::uint64_t* out, std::uint32_t* overflow,
+                           void* scratch, cudaStream_t s, int sms);
+
+}  // namespace cb

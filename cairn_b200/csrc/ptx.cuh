@@ -1,0 +1,191 @@
+// Thin inline-PTX wrappers for the sm_100a features the kernels use: mbarriers with bounded waits, TMA tensor loads,
+// and the tcgen05 family (TMEM allocation, UMMA issue, commit, TMEM loads). Every wait in this library is bounded:
+// after WAIT_LIMIT_NS of polling it records a fault in the kernel's fault word, raises the block's abort flag, and
+// returns false, so a kernel whose partner never arrives ends with an error status instead of hanging the GPU.
+#pragma once
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace cb {
+
+// How long a device-side wait polls before it gives up (2 s of %globaltimer).
+constexpr std::uint64_t WAIT_LIMIT_NS = 2000000000ull;
+
+// Fault codes a kernel ORs into its fault word. The host maps any nonzero word to CAIRN_B200_ERR_TIMEOUT.
+enum Fault : std::uint32_t {
+  FAULT_WAIT_FULL = 1u << 0,    // the MMA issuer waited for a stage's TMA load
+  FAULT_WAIT_EMPTY = 1u << 1,   // the producer waited for a stage to be consumed
+  FAULT_WAIT_TFULL = 1u << 2,   // an epilogue warp waited for an accumulator
+  FAULT_WAIT_TEMPTY = 1u << 3,  // the MMA issuer waited for an accumulator to be drained
+  FAULT_DRAIN = 1u << 4,        // the exit path waited for copies or MMAs still in flight
+};
+
+__device__ __forceinline__ std::uint64_t globaltimer() {
+  std::uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ std::uint32_t smem_u32(const void* p) {
+  return static_cast<std::uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// mbarrier
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void mbar_init(std::uint64_t* bar, std::uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+// Makes initialised barriers visible to the async proxy (TMA, tcgen05) before any thread uses them.
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(std::uint64_t* bar, std::uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(std::uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// True once the phase of parity `parity` has completed.
+__device__ __forceinline__ bool mbar_test(std::uint64_t* bar, std::uint32_t parity) {
+  std::uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// The slow half of a bounded wait: polls until the phase completes, the block's abort flag rises, or the limit
+// passes (then records `fault`, raises the flag and gives up).
+__device__ __noinline__ inline bool mbar_wait_slow(std::uint64_t* bar, std::uint32_t parity,
+                                                   volatile std::uint32_t* abort_flag, std::uint32_t* fault_word,
+                                                   std::uint32_t fault) {
+  const std::uint64_t start = globaltimer();
+  for (std::uint32_t spin = 1;; ++spin) {
+    if (mbar_test(bar, parity)) return true;
+    if ((spin & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - start > WAIT_LIMIT_NS) {
+        atomicOr(fault_word, fault);
+        *abort_flag = 1u;
+        __threadfence_block();
+        return false;
+      }
+    }
+  }
+}
+__device__ __forceinline__ bool mbar_wait(std::uint64_t* bar, std::uint32_t parity, volatile std::uint32_t* abort_flag,
+                                          std::uint32_t* fault_word, std::uint32_t fault) {
+  if (mbar_test(bar, parity)) return true;
+  return mbar_wait_slow(bar, parity, abort_flag, fault_word, fault);
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// TMA (bulk tensor copies, global -> shared, completion counted on an mbarrier). No multicast anywhere.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<std::uint64_t>(map)) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(std::uint32_t dst, const CUtensorMap* map, std::uint64_t* bar,
+                                            std::int32_t x, std::int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          dst),
+      "l"(reinterpret_cast<std::uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// tcgen05: tensor memory and the 5th-generation MMA (single-CTA group)
+// ---------------------------------------------------------------------------------------------------------------
+// Warp-wide: allocates `cols` TMEM columns and writes their base address to the shared slot.
+__device__ __forceinline__ void tmem_alloc(std::uint32_t* slot, std::uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(std::uint32_t taddr, std::uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+// Arrives once on `bar` when every tcgen05 operation this thread issued before it has completed.
+__device__ __forceinline__ void tc_commit(std::uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// The MMA kinds this library issues.
+enum MmaKind : int { KIND_F16 = 0, KIND_TF32 = 1, KIND_F8F6F4 = 2 };
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]; `accumulate` 0 overwrites D.
+template <int KIND>
+__device__ __forceinline__ void umma(std::uint32_t d_tmem, std::uint64_t a_desc, std::uint64_t b_desc,
+                                     std::uint32_t idesc, std::uint32_t accumulate) {
+  if constexpr (KIND == KIND_F16) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  } else if constexpr (KIND == KIND_TF32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  }
+}
+
+// 32 TMEM lanes x 32 consecutive 32-bit columns: lane i of the warp receives TMEM lane (base lane + i), columns
+// [col, col + 32) in r[0..31]. Warp-collective; follow with tmem_wait_ld before reading r.
+__device__ __forceinline__ void tmem_ld_32x32b_x32(std::uint32_t taddr, std::uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------------------------------
+// UMMA descriptors (the sm_100 shared-memory matrix descriptor and the kind::f16/tf32/f8f6f4 instruction descriptor)
+// ---------------------------------------------------------------------------------------------------------------
+// Shared-memory matrix descriptor for a 128-byte-swizzled tile: start address, leading- and stride-dimension byte
+// offsets (all in 16-byte units), version 1 (sm_100) at bit 46, swizzle mode 2 (128B) at bits 61-63. The tile's
+// swizzle atoms (8 rows x 128 bytes) start on 1024-byte boundaries, so the base-offset field stays 0.
+__device__ __forceinline__ std::uint64_t sdesc_sw128(std::uint32_t saddr, std::uint32_t lbo_bytes,
+                                                     std::uint32_t sbo_bytes) {
+  std::uint64_t d = 0;
+  d |= static_cast<std::uint64_t>((saddr >> 4) & 0x3fffu);
+  d |= static_cast<std::uint64_t>((lbo_bytes >> 4) & 0x3fffu) << 16;
+  d |= static_cast<std::uint64_t>((sbo_bytes >> 4) & 0x3fffu) << 32;
+  d |= 1ull << 46;
+  d |= 2ull << 61;
+  return d;
+}
+
+// Instruction descriptor: D format f32 (bits 4-5 = 1), A and B formats (bits 7-9, 10-12), A/B major-ness (bit 15:
+// A is MN-major, bit 16: B is MN-major), N >> 3 (bits 17-22), M >> 4 (bits 24-28).
+__host__ __device__ constexpr std::uint32_t idesc_make(std::uint32_t a_fmt, std::uint32_t b_fmt, bool a_mn, bool b_mn,
+                                                       std::uint32_t m, std::uint32_t n) {
+  return (1u << 4) | (a_fmt << 7) | (b_fmt << 10) | (static_cast<std::uint32_t>(a_mn) << 15) |
+         (static_cast<std::uint32_t>(b_mn) << 16) | ((n >> 3) << 17) | ((m >> 4) << 24);
+}
+
+}  // namespace cb

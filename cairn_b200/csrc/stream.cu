@@ -1,0 +1,386 @@
+// The bandwidth-bound half of the hot path: the `parallel` saxpy region and the `reduce +` collectors over f32 and
+// u64, rebuilt for sm_100a.
+//
+// The reference runs a `parallel` region as one index per thread in a grid of at most 65535 blocks of 256 threads,
+// scalar 4-byte accesses (runtime/cairn_kernels.hpp:69-96), and a device `reduce +` through CUB's DeviceReduce with
+// temporaries from the context's arena (runtime/cairn_reuse.hpp:346-372, runtime/cairn_cub.hpp:14-17). Here:
+//   - a grid of 2 x 512-thread blocks per SM (every SM holds 1024 threads), grid-stride over 16-byte vectors, four
+//     vectors of each operand in flight per thread, streaming cache hints (each byte is touched once);
+//   - the reductions fold each thread's terms into registers, then a warp shuffle tree, a shared-memory tree across
+//     the block's 16 warps, one partial per block in scratch, and the last block to finish (an atomic ticket, no
+//     spin-wait) folds the partials in block order and writes the total. One launch, deterministic for a given n
+//     and device: every thread's terms and every tree are fixed by (n, grid).
+//   - f32 terms are added in f64, which holds every f32 term exactly; the total is rounded to f32 once.
+//   - u64 terms carry cr::Sum's sticky overflow flag (runtime/cairn_runtime.hpp:158-166) through every fold.
+#include <cstdint>
+#include <cuda_runtime.h>
+#include "gemm.h"
+
+namespace cb {
+
+int stream_grid(int sms) { return 2 * sms; }
+// One 32-byte partial per block, then the ticket (zero between launches).
+std::size_t reduce_scratch_bytes(int sms) { return static_cast<std::size_t>(stream_grid(sms)) * 32 + 256; }
+
+namespace {
+
+constexpr int T = STREAM_THREADS;
+constexpr int WARPS = T / 32;
+constexpr int UNROLL = 4;
+
+__device__ __forceinline__ float saxpy1(float a, float x, float y) { return __fadd_rn(__fmul_rn(a, x), y); }
+
+// out may equal x or y: each vector is read before the same vector is written.
+__global__ void __launch_bounds__(T, 2)
+    saxpy_vec_kernel(std::size_t n, float* out, const float* x, const float* y, float a) {
+  const std::size_t n4 = n / 4;
+  const std::size_t stride = static_cast<std::size_t>(gridDim.x) * T;
+  std::size_t i = static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x;
+  const float4* x4 = reinterpret_cast<const float4*>(x);
+  const float4* y4 = reinterpret_cast<const float4*>(y);
+  float4* o4 = reinterpret_cast<float4*>(out);
+  for (; i + (UNROLL - 1) * stride < n4; i += UNROLL * stride) {
+    float4 xv[UNROLL], yv[UNROLL];
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      xv[u] = __ldcs(x4 + i + u * stride);
+      yv[u] = __ldcs(y4 + i + u * stride);
+    }
+#pragma unroll
+    for (int u = 0; u < UNROLL; ++u) {
+      const float4 o = make_float4(saxpy1(a, xv[u].x, yv[u].x), saxpy1(a, xv[u].y, yv[u].y),
+                                   saxpy1(a, xv[u].z, yv[u].z), saxpy1(a, xv[u].w, yv[u].w));
+      __stcs(o4 + i + u * stride, o);
+    }
+  }
+  for (; i < n4; i += stride) {
+    const float4 xv = __ldcs(x4 + i), yv = __ldcs(y4 + i);
+    __stcs(o4 + i, make_float4(saxpy1(a, xv.x, yv.x), saxpy1(a, xv.y, yv.y), saxpy1(a, xv.z, yv.z),
+                               saxpy1(a, xv.w, yv.w)));
+  }
+  if (blockIdx.x == 0 && threadIdx.x < n - n4 * 4) {
+    const std::size_t j = n4 * 4 + threadIdx.x;
+    out[j] = saxpy1(a, x[j], y[j]);
+  }
+}
+
+__global__ void __launch_bounds__(T, 2)
+    saxpy_scalar_kernel(std::size_t n, float* out, const float* x, const float* y, float a) {
+  const std::size_t stride = static_cast<std::size_t>(gridDim.x) * T;
+  for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x; i < n; i += stride)
+    out[i] = saxpy1(a, x[i], y[i]);
+}
+
+// ---- f32 sum --------------------------------------------------------------------------------------------------
+// The host's `reduce + parallel` over f32 is the exact sum rounded once (runtime/cairn_sum.hpp:1-17). The device
+// keeps that answer: each thread runs four double-double accumulators (s, c), where Knuth's TwoSum adds a term to s
+// and moves the rounding error, exactly, into c; the trees combine double-doubles the same way, and the total is
+// rounded to f32 from the double-double with the tie decided by its low part. A term that is an infinity or a NaN
+// leaves a non-finite s or c, and only such a term does (finite f32 terms cannot overflow f64); such a thread looks
+// at its terms again for the flags cr::sum::result reads (runtime/cairn_sum.hpp:186-195). OTHER marks a term that is
+// not -0.0: an exact zero total is -0.0 only when every term was.
+enum : unsigned { SUM_NAN = 1, SUM_PINF = 2, SUM_NINF = 4, SUM_OTHER = 8, SUM_SOME = 16 };
+
+struct DD {
+  double s, c;
+};
+struct Partial {  // one block's part, in scratch (32 bytes)
+  double s, c;
+  unsigned flags, pad[3];
+};
+
+__device__ __forceinline__ void two_sum_into(double& s, double& c, double x) {
+  const double t = __dadd_rn(s, x);
+  const double z = __dsub_rn(t, s);
+  c = __dadd_rn(c, __dadd_rn(__dsub_rn(s, __dsub_rn(t, z)), __dsub_rn(x, z)));
+  s = t;
+}
+__device__ __forceinline__ DD dd_add(DD p, DD q) {
+  double s = p.s, c = __dadd_rn(p.c, q.c);
+  two_sum_into(s, c, q.s);
+  return {s, c};
+}
+__device__ __forceinline__ DD warp_dd(DD v) {
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    DD o;
+    o.s = __shfl_xor_sync(0xffffffffu, v.s, off);
+    o.c = __shfl_xor_sync(0xffffffffu, v.c, off);
+    v = dd_add(v, o);
+  }
+  return v;
+}
+__device__ __forceinline__ unsigned warp_or(unsigned f) {
+#pragma unroll
+  for (int off = 16; off; off >>= 1) f |= __shfl_xor_sync(0xffffffffu, f, off);
+  return f;
+}
+// The block's double-double and flags, held by every thread of warp 0 on return.
+__device__ __forceinline__ void block_dd(DD& v, unsigned& flags, DD* sv, unsigned* sf) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  v = warp_dd(v);
+  flags = warp_or(flags);
+  if (lane == 0) {
+    sv[warp] = v;
+    sf[warp] = flags;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    v = lane < WARPS ? sv[lane] : DD{-0.0, -0.0};
+    flags = lane < WARPS ? sf[lane] : 0u;
+    v = warp_dd(v);
+    flags = warp_or(flags);
+  }
+  __syncthreads();
+}
+
+// The f32 nearest (ties to even) to the exact value hi + lo, where hi = RN(hi + lo) in f64.
+__device__ float round_dd_f32(double hi, double lo) {
+  const float f = __double2float_rn(hi);
+  if (lo == 0.0) return f;
+  if (isinf(f)) {  // hi is at or past the overflow threshold: only the threshold itself can still go back down
+    const double threshold = 3.4028235677973366e38;  // FLT_MAX + 2^103, the midpoint to 2^128
+    return (fabs(hi) == threshold && ((lo < 0.0) == (hi > 0.0))) ? copysignf(3.4028234663852886e38f, f) : f;
+  }
+  const double fd = static_cast<double>(f);
+  if (fd == hi) return f;  // |lo| is below half an f64 ulp of hi, far below half an f32 ulp
+  const float g = hi > fd ? nextafterf(f, INFINITY) : nextafterf(f, -INFINITY);
+  const double gd = static_cast<double>(g);
+  if (__dsub_rn(hi, fd) == __dsub_rn(gd, hi)) return ((lo > 0.0) == (gd > fd)) ? g : f;  // hi is the midpoint
+  return f;
+}
+
+template <bool VEC, class F>
+__device__ __forceinline__ void for_terms(std::size_t n, const float* x, F&& term) {
+  const std::size_t stride = static_cast<std::size_t>(gridDim.x) * T;
+  std::size_t i = static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x;
+  if constexpr (VEC) {
+    const std::size_t n4 = n / 4;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    for (; i + (UNROLL - 1) * stride < n4; i += UNROLL * stride) {
+      float4 v[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) v[u] = __ldcs(x4 + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        term(0, v[u].x);
+        term(1, v[u].y);
+        term(2, v[u].z);
+        term(3, v[u].w);
+      }
+    }
+    for (; i < n4; i += stride) {
+      const float4 v = __ldcs(x4 + i);
+      term(0, v.x);
+      term(1, v.y);
+      term(2, v.z);
+      term(3, v.w);
+    }
+    i = n4 * 4 + static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x;
+  }
+  for (; i < n; i += stride) term(0, __ldcs(x + i));
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(T, 2) sum_f32_kernel(std::size_t n, const float* x, float* out_f32,
+                                                      double* out_f64, Partial* partials, unsigned int* ticket) {
+  __shared__ DD sv[WARPS];
+  __shared__ unsigned sf[WARPS];
+  __shared__ bool last;
+  // -0.0 is the identity of IEEE addition: a chain that only ever adds -0.0 terms stays -0.0.
+  double s[4] = {-0.0, -0.0, -0.0, -0.0}, c[4] = {-0.0, -0.0, -0.0, -0.0};
+  for_terms<VEC>(n, x, [&](int q, float v) { two_sum_into(s[q], c[q], static_cast<double>(v)); });
+  unsigned flags = 0;
+  bool special = false;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    special |= !isfinite(s[q]) || !isfinite(c[q]);
+    if (__double_as_longlong(s[q]) != static_cast<long long>(0x8000000000000000ull)) flags |= SUM_OTHER;
+  }
+  DD v = dd_add(dd_add(DD{s[0], c[0]}, DD{s[1], c[1]}), dd_add(DD{s[2], c[2]}, DD{s[3], c[3]}));
+  if (special) {  // an infinity or a NaN among this thread's terms: read them again for the flags
+    for_terms<VEC>(n, x, [&](int, float t) {
+      const unsigned u = __float_as_uint(t);
+      if ((u & 0x7f800000u) == 0x7f800000u) flags |= (u & 0x7fffffu) ? SUM_NAN : ((u >> 31) ? SUM_NINF : SUM_PINF);
+    });
+    v = DD{0.0, 0.0};
+  }
+  block_dd(v, flags, sv, sf);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x].s = v.s;
+    partials[blockIdx.x].c = v.c;
+    partials[blockIdx.x].flags = flags;
+    __threadfence();
+    last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  DD t{-0.0, -0.0};
+  unsigned tf = 0;
+  for (unsigned int b = threadIdx.x; b < gridDim.x; b += T) {
+    t = dd_add(t, DD{__ldcg(&partials[b].s), __ldcg(&partials[b].c)});
+    tf |= __ldcg(&partials[b].flags);
+  }
+  block_dd(t, tf, sv, sf);
+  if (threadIdx.x == 0) {
+    // hi + lo = s + c exactly, with hi = RN(s + c) (TwoSum: s and c may be of either size after cancellation)
+    const double hi = __dadd_rn(t.s, t.c);
+    const double z = __dsub_rn(hi, t.s);
+    const double lo = __dadd_rn(__dsub_rn(t.s, __dsub_rn(hi, z)), __dsub_rn(t.c, z));
+    float r;
+    if ((tf & SUM_NAN) || ((tf & SUM_PINF) && (tf & SUM_NINF))) r = __uint_as_float(0x7fc00000u);
+    else if (tf & SUM_PINF) r = __uint_as_float(0x7f800000u);
+    else if (tf & SUM_NINF) r = __uint_as_float(0xff800000u);
+    else if (hi == 0.0) r = (tf & SUM_OTHER) ? 0.0f : -0.0f;
+    else r = round_dd_f32(hi, lo);
+    if (out_f32) out_f32[0] = r;
+    if (out_f64) {  // the unrounded part for a sharded sum: hi, lo and the flags (SUM_SOME: n > 0)
+      out_f64[0] = hi;
+      out_f64[1] = lo;
+      out_f64[2] = static_cast<double>(tf | SUM_SOME);
+    }
+    *ticket = 0u;  // ready for the next launch that uses this scratch
+  }
+}
+
+// ---- u64 checked sum --------------------------------------------------------------------------------------------
+struct SumU64 {
+  unsigned long long v;
+  unsigned int over;
+};
+__device__ __forceinline__ SumU64 fold(SumU64 p, SumU64 q) {
+  const unsigned long long s = p.v + q.v;
+  return {s, p.over | q.over | (s < p.v ? 1u : 0u)};
+}
+__device__ __forceinline__ SumU64 warp_fold(SumU64 s) {
+#pragma unroll
+  for (int off = 16; off; off >>= 1) {
+    SumU64 o;
+    o.v = __shfl_xor_sync(0xffffffffu, s.v, off);
+    o.over = __shfl_xor_sync(0xffffffffu, s.over, off);
+    s = fold(s, o);
+  }
+  return s;
+}
+__device__ __forceinline__ SumU64 block_fold(SumU64 s, SumU64* shared) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  s = warp_fold(s);
+  if (lane == 0) shared[warp] = s;
+  __syncthreads();
+  SumU64 t{0ull, 0u};
+  if (warp == 0) {
+    if (lane < WARPS) t = shared[lane];
+    t = warp_fold(t);
+  }
+  __syncthreads();
+  return t;
+}
+__device__ __forceinline__ void add_term(SumU64& s, unsigned long long x) {
+  s.v += x;
+  s.over |= s.v < x ? 1u : 0u;
+}
+
+template <bool VEC>
+__global__ void __launch_bounds__(T, 2) sum_u64_kernel(std::size_t n, const unsigned long long* x,
+                                                      unsigned long long* out, unsigned int* overflow,
+                                                      SumU64* partials, unsigned int* ticket) {
+  __shared__ SumU64 shared[WARPS];
+  __shared__ bool last;
+  const std::size_t stride = static_cast<std::size_t>(gridDim.x) * T;
+  std::size_t i = static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x;
+  SumU64 s0{0ull, 0u}, s1{0ull, 0u};
+  if constexpr (VEC) {
+    const std::size_t n2 = n / 2;
+    const ulonglong2* x2 = reinterpret_cast<const ulonglong2*>(x);
+    for (; i + (UNROLL - 1) * stride < n2; i += UNROLL * stride) {
+      ulonglong2 v[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) v[u] = __ldcs(x2 + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        add_term(s0, v[u].x);
+        add_term(s1, v[u].y);
+      }
+    }
+    for (; i < n2; i += stride) {
+      const ulonglong2 v = __ldcs(x2 + i);
+      add_term(s0, v.x);
+      add_term(s1, v.y);
+    }
+    i = n2 * 2 + static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x;
+  }
+  for (; i < n; i += stride) add_term(s0, __ldcs(x + i));
+  SumU64 s = block_fold(fold(s0, s1), shared);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = s;
+    __threadfence();
+    last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  SumU64 t{0ull, 0u};
+  for (unsigned int b = threadIdx.x; b < gridDim.x; b += T) {
+    SumU64 p;
+    p.v = __ldcg(&partials[b].v);
+    p.over = __ldcg(&partials[b].over);
+    t = fold(t, p);
+  }
+  t = block_fold(t, shared);
+  if (threadIdx.x == 0) {
+    *out = t.v;
+    *overflow = t.over;
+    *ticket = 0u;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+cudaError_t saxpy_f32_launch(std::size_t n, float* out, const float* x, const float* y, float a, cudaStream_t s,
+                             int sms) {
+  if (!n) return cudaSuccess;
+  const int grid = stream_grid(sms);
+  if (aligned16(out) && aligned16(x) && aligned16(y)) saxpy_vec_kernel<<<grid, T, 0, s>>>(n, out, x, y, a);
+  else saxpy_scalar_kernel<<<grid, T, 0, s>>>(n, out, x, y, a);
+  return cudaGetLastError();
+}
+
+cudaError_t sum_f32_launch(std::size_t n, const float* x, float* out_f32, double* out_f64, void* scratch,
+                           cudaStream_t s, int sms) {
+  if (!n) {  // the empty sum is +0.0 (cr::sum::result with n == 0), and its part is (0, 0, no flags)
+    if (out_f32) {
+      const cudaError_t e = cudaMemsetAsync(out_f32, 0, sizeof(float), s);
+      if (e != cudaSuccess) return e;
+    }
+    if (out_f64) return cudaMemsetAsync(out_f64, 0, 3 * sizeof(double), s);
+    return cudaSuccess;
+  }
+  const int grid = stream_grid(sms);
+  Partial* partials = static_cast<Partial*>(scratch);
+  unsigned int* ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(scratch) + static_cast<std::size_t>(grid) * 32);
+  if (aligned16(x)) sum_f32_kernel<true><<<grid, T, 0, s>>>(n, x, out_f32, out_f64, partials, ticket);
+  else sum_f32_kernel<false><<<grid, T, 0, s>>>(n, x, out_f32, out_f64, partials, ticket);
+  return cudaGetLastError();
+}
+
+cudaError_t sum_u64_launch(std::size_t n, const std::uint64_t* x, std::uint64_t* out, std::uint32_t* overflow,
+                           void* scratch, cudaStream_t s, int sms) {
+  if (!n) {
+    cudaError_t e = cudaMemsetAsync(out, 0, sizeof(std::uint64_t), s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(overflow, 0, sizeof(std::uint32_t), s);
+    return e;
+  }
+  const int grid = stream_grid(sms);
+  SumU64* partials = static_cast<SumU64*>(scratch);
+  unsigned int* ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(scratch) + static_cast<std::size_t>(grid) * 32);
+  const auto* xx = reinterpret_cast<const unsigned long long*>(x);
+  auto* oo = reinterpret_cast<unsigned long long*>(out);
+  if (aligned16(x)) sum_u64_kernel<true><<<grid, T, 0, s>>>(n, xx, oo, overflow, partials, ticket);
+  else sum_u64_kernel<false><<<grid, T, 0, s>>>(n, xx, oo, overflow, partials, ticket);
+  return cudaGetLastError();
+}
+
+}  // namespace cb

@@ -1,0 +1,247 @@
+"""TEST INFRASTRUCTURE ONLY: the CPU oracle of the cairn_b200 parity tests.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg (and its reference arm) import this package,
+and only as the checker or the timed CPU baseline; the cairn_b200 package never does.
+
+  restated   numpy wrappers of liboracle.so, the C restatement in cairn_oracle.c (each function cites the
+             reference file:line it restates)
+  reference  numpy wrappers of _ref/libcairn_ref.so, the reference's own header-only host path compiled from its
+             sources by the Makefile here (present where the reference tree was available at build time)
+  exact_sum_f32_bits  a pure-Python model of the correctly rounded sum (Fraction arithmetic) for small cases
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import math
+import struct
+import subprocess
+from fractions import Fraction
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+RESTATED = HERE / "liboracle.so"
+REFERENCE = HERE / "_ref" / "libcairn_ref.so"
+
+_z, _p, _f = C.c_size_t, C.c_void_p, C.c_float
+
+
+def build(reference_runtime: str | None = None) -> None:
+    """make -C oracle [REF=...]: the restatement always, the reference's host path when its runtime dir is given."""
+    cmd = ["make", "-s", "-C", str(HERE)]
+    if reference_runtime:
+        cmd.append(f"REF={reference_runtime}")
+    subprocess.run(cmd, check=True)
+
+
+def _ptr(a: np.ndarray) -> int:
+    return a.ctypes.data
+
+
+class _Lib:
+    def __init__(self, path: Path, prefix: str):
+        self.path, self.prefix, self._h = path, prefix, None
+
+    def available(self) -> bool:
+        return self.path.exists()
+
+    def h(self) -> C.CDLL:
+        if self._h is None:
+            if not self.path.exists():
+                if self.path == RESTATED:
+                    build()
+                else:
+                    raise FileNotFoundError(f"{self.path} is not built (it needs the reference source tree)")
+            self._h = C.CDLL(str(self.path))
+        return self._h
+
+    def fn(self, name: str, res, args):
+        f = getattr(self.h(), self.prefix + name)
+        f.restype, f.argtypes = res, args
+        return f
+
+
+_rest = _Lib(RESTATED, "oracle_")
+_ref = _Lib(REFERENCE, "ref_")
+
+MMA_DTYPES = {"bf16": np.uint16, "f16": np.uint16, "f8e4m3": np.uint8, "f8e5m2": np.uint8, "f32": np.float32}
+
+
+class restated:
+    """The C restatement (cairn_oracle.c)."""
+
+    @staticmethod
+    def mma(fmt: str, c: np.ndarray, a: np.ndarray, b: np.ndarray, m: int, n: int, k: int) -> np.ndarray:
+        """c (f32, m*n) += a * b in the reference's order; returns a new array."""
+        name = {"bf16": "mma_bf16", "f16": "mma_f16", "f8e4m3": "mma_e4m3", "f8e5m2": "mma_e5m2", "f32": "mma_f32"}[fmt]
+        out = np.ascontiguousarray(c, dtype=np.float32).copy()
+        a = np.ascontiguousarray(a, dtype=MMA_DTYPES[fmt])
+        b = np.ascontiguousarray(b, dtype=MMA_DTYPES[fmt])
+        _rest.fn(name, None, [_z, _z, _z, _p, _p, _p])(m, n, k, _ptr(out), _ptr(a), _ptr(b))
+        return out
+
+    @staticmethod
+    def mma_bf16_rows(a: np.ndarray, b: np.ndarray, m: int, n: int, k: int, r0: int, r1: int,
+                      c_rows: np.ndarray | None = None) -> np.ndarray:
+        out = np.zeros((r1 - r0) * n, np.float32) if c_rows is None else np.ascontiguousarray(c_rows, np.float32).copy()
+        a = np.ascontiguousarray(a, np.uint16)
+        b = np.ascontiguousarray(b, np.uint16)
+        _rest.fn("mma_bf16_rows", None, [_z, _z, _z, _z, _z, _p, _p, _p])(m, n, k, r0, r1, _ptr(out), _ptr(a), _ptr(b))
+        return out
+
+    @staticmethod
+    def gemm_t16(c: np.ndarray, a: np.ndarray, b: np.ndarray, m: int, n: int, k: int, trans_a: bool, trans_b: bool,
+                 fmt: str = "bf16") -> np.ndarray:
+        out = np.ascontiguousarray(c, np.float32).copy()
+        a = np.ascontiguousarray(a, np.uint16)
+        b = np.ascontiguousarray(b, np.uint16)
+        _rest.fn("gemm_t16", None, [_z, _z, _z, _p, _p, _p, C.c_int, C.c_int, C.c_int])(
+            m, n, k, _ptr(out), _ptr(a), _ptr(b), int(trans_a), int(trans_b), 1 if fmt == "f16" else 0)
+        return out
+
+    @staticmethod
+    def bias_act(acc: np.ndarray, bias: np.ndarray | None, relu: bool, m: int, n: int) -> np.ndarray:
+        acc = np.ascontiguousarray(acc, np.float32)
+        out = np.empty(m * n, np.uint16)
+        bias_c = None if bias is None else np.ascontiguousarray(bias, np.float32)
+        _rest.fn("bias_act", None, [_z, _z, _p, _p, C.c_int, _p])(
+            m, n, _ptr(acc), None if bias_c is None else _ptr(bias_c), int(relu), _ptr(out))
+        return out
+
+    @staticmethod
+    def sum_f32(x: np.ndarray) -> np.float32:
+        x = np.ascontiguousarray(x, np.float32)
+        return np.float32(_rest.fn("sum_f32", _f, [_z, _p])(x.size, _ptr(x)))
+
+    @staticmethod
+    def sum_u64(x: np.ndarray) -> tuple[int, bool]:
+        x = np.ascontiguousarray(x, np.uint64)
+        over = C.c_int(0)
+        v = _rest.fn("sum_u64", C.c_uint64, [_z, _p, C.POINTER(C.c_int)])(x.size, _ptr(x), C.byref(over))
+        return int(v), bool(over.value)
+
+    @staticmethod
+    def saxpy(a: float, x: np.ndarray, y: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.ascontiguousarray(y, np.float32)
+        out = np.empty_like(x)
+        _rest.fn("saxpy_f32", None, [_z, _p, _p, _p, _f])(x.size, _ptr(out), _ptr(x), _ptr(y), a)
+        return out
+
+    @staticmethod
+    def widen(fmt: str, bits: np.ndarray) -> np.ndarray:
+        name = {"bf16": "bf16_to_f32", "f16": "f16_to_f32", "f8e4m3": "e4m3_to_f32", "f8e5m2": "e5m2_to_f32"}[fmt]
+        argt = C.c_uint16 if fmt in ("bf16", "f16") else C.c_uint8
+        f = _rest.fn(name, _f, [argt])
+        return np.array([f(int(v)) for v in np.asarray(bits).ravel()], np.float32)
+
+    @staticmethod
+    def f32_to_bf16(x: np.ndarray) -> np.ndarray:
+        f = _rest.fn("f32_to_bf16", C.c_uint16, [_f])
+        return np.array([f(float(v)) for v in np.asarray(x, np.float32).ravel()], np.uint16)
+
+
+class reference:
+    """The reference's own host path (ref_shim.cpp over the CAIRN runtime headers)."""
+
+    @staticmethod
+    def available() -> bool:
+        return _ref.available()
+
+    @staticmethod
+    def mma(fmt: str, c: np.ndarray, a: np.ndarray, b: np.ndarray, m: int, n: int, k: int) -> np.ndarray:
+        out = np.ascontiguousarray(c, np.float32).copy()
+        a = np.ascontiguousarray(a, MMA_DTYPES[fmt])
+        b = np.ascontiguousarray(b, MMA_DTYPES[fmt])
+        _ref.fn(f"mma_{fmt}", None, [_z, _z, _z, _p, _p, _p])(m, n, k, _ptr(out), _ptr(a), _ptr(b))
+        return out
+
+    @staticmethod
+    def mma_bf16_pooled(c: np.ndarray, a: np.ndarray, b: np.ndarray, m: int, n: int, k: int) -> np.ndarray:
+        out = np.ascontiguousarray(c, np.float32).copy()
+        _ref.fn("mma_bf16_pooled", None, [_z, _z, _z, _p, _p, _p])(
+            m, n, k, _ptr(out), _ptr(np.ascontiguousarray(a, np.uint16)), _ptr(np.ascontiguousarray(b, np.uint16)))
+        return out
+
+    @staticmethod
+    def gemm_f32_region(c: np.ndarray, a: np.ndarray, b: np.ndarray, m: int, n: int, k: int) -> np.ndarray:
+        out = np.ascontiguousarray(c, np.float32).copy()
+        _ref.fn("gemm_f32_region", None, [_z, _z, _z, _p, _p, _p])(
+            m, n, k, _ptr(out), _ptr(np.ascontiguousarray(a, np.float32)), _ptr(np.ascontiguousarray(b, np.float32)))
+        return out
+
+    @staticmethod
+    def sum_f32(x: np.ndarray) -> np.float32:
+        x = np.ascontiguousarray(x, np.float32)
+        return np.float32(_ref.fn("sum_f32", _f, [_z, _p])(x.size, _ptr(x)))
+
+    @staticmethod
+    def sum_u64(x: np.ndarray) -> tuple[int, bool]:
+        x = np.ascontiguousarray(x, np.uint64)
+        over = C.c_int(0)
+        v = _ref.fn("sum_u64", C.c_uint64, [_z, _p, C.POINTER(C.c_int)])(x.size, _ptr(x), C.byref(over))
+        return int(v), bool(over.value)
+
+    @staticmethod
+    def saxpy(a: float, x: np.ndarray, y: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.ascontiguousarray(y, np.float32)
+        out = np.empty_like(x) if out is None else out
+        _ref.fn("saxpy_f32", None, [_z, _p, _p, _p, _f])(x.size, _ptr(out), _ptr(x), _ptr(y), a)
+        return out
+
+    @staticmethod
+    def widen(fmt: str, bits: np.ndarray) -> np.ndarray:
+        argt = C.c_uint16 if fmt in ("bf16", "f16") else C.c_uint8
+        f = _ref.fn(f"widen_{fmt}", _f, [argt])
+        return np.array([f(int(v)) for v in np.asarray(bits).ravel()], np.float32)
+
+    @staticmethod
+    def narrow_bf16(x: float) -> int:
+        return int(_ref.fn("narrow_bf16", C.c_uint16, [C.c_double])(x))
+
+    @staticmethod
+    def lanes() -> int:
+        return int(_ref.fn("lanes", _z, [])())
+
+
+# ---- a pure-Python model of the correctly rounded f32 sum (for small cases) ----------------------------------------
+def _f32_bits(x: float) -> int:
+    return struct.unpack("<I", struct.pack("<f", x))[0]
+
+
+def exact_sum_f32_bits(terms: list[float]) -> int:
+    """The pattern of the f32 exact sum of f32 `terms`, rounded once to nearest-even, with cr::sum::result's rules
+    for NaN, infinities and the sign of an exact zero (runtime/cairn_sum.hpp:186-195)."""
+    if any(t != t for t in terms) or (math.inf in terms and -math.inf in terms):
+        return 0x7FC00000
+    if math.inf in terms:
+        return 0x7F800000
+    if -math.inf in terms:
+        return 0xFF800000
+    total = sum((Fraction(t) for t in terms), Fraction(0))
+    if total == 0:
+        return 0x80000000 if terms and all(_f32_bits(t) == 0x80000000 for t in terms) else 0
+    sign = 0x80000000 if total < 0 else 0
+    mag = abs(total)
+    e = mag.numerator.bit_length() - mag.denominator.bit_length()
+    while Fraction(2) ** e > mag:
+        e -= 1
+    while Fraction(2) ** (e + 1) <= mag:
+        e += 1
+    q = max(e, -126) - 23
+    scaled = mag / Fraction(2) ** q
+    m, rest = divmod(scaled.numerator, scaled.denominator)
+    if 2 * rest > scaled.denominator or (2 * rest == scaled.denominator and m % 2 == 1):
+        m += 1
+    if m == 1 << 24:
+        m >>= 1
+        q += 1
+    if m < 1 << 23:
+        return sign | m
+    exponent = q + 23
+    if exponent > 127:
+        return sign | 0x7F800000
+    return sign | ((exponent + 127) << 23) | (m & 0x7FFFFF)

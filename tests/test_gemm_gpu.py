@@ -1,0 +1,205 @@
+"""The tensor-core multiply on the B200 against the CPU oracle, through the C ABI.
+
+The bar is the reference's own device test (tests/soundness/test_tensor.py:182-226): every output within 2x the
+contract bound (k + 1) * 2^-22 * (|c| + sum |a * b|) of the host reference, on its shapes (tails in every direction,
+empty extents). Beyond it: the golden fixtures of the reference's own host multiply, the transposed operands of the
+dense layer's backward, the fused bias/ReLU/bf16 epilogue, tf32, and the BASELINE 4096^3 product on sampled rows
+within the north star's 2e-2 Frobenius tolerance. Two runs on one device give the same bits (docs/numerics.md: "Two
+runs on one device give the same bits").
+"""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import cairn_b200
+import inputs
+from oracle import restated
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TORCH = {"bf16": torch.bfloat16, "f16": torch.float16, "f8e4m3": torch.float8_e4m3fn, "f8e5m2": torch.float8_e5m2}
+BITS = {"bf16": torch.int16, "f16": torch.int16, "f8e4m3": torch.uint8, "f8e5m2": torch.uint8}
+
+
+def to_dev(fmt: str, bits: np.ndarray, dev) -> torch.Tensor:
+    t = torch.from_numpy(np.ascontiguousarray(bits).view(np.int16 if inputs.WIDTH[fmt] == 16 else np.uint8).copy())
+    return t.to(dev).view(TORCH[fmt])
+
+
+def bound(fmt: str, c: np.ndarray, a: np.ndarray, b: np.ndarray, m: int, n: int, k: int) -> np.ndarray:
+    av = np.abs(inputs.decode(fmt, a).reshape(m, k)) if fmt != "f32" else np.abs(a.reshape(m, k).astype(np.float64))
+    bv = np.abs(inputs.decode(fmt, b).reshape(k, n)) if fmt != "f32" else np.abs(b.reshape(k, n).astype(np.float64))
+    return (k + 1) * 2.0**-22 * (np.abs(c.reshape(m, n).astype(np.float64)) + av @ bv)
+
+
+def device_mma(fmt: str, c: np.ndarray, a: np.ndarray, b: np.ndarray, m: int, n: int, k: int, dev) -> np.ndarray:
+    ct = torch.from_numpy(c.copy()).to(dev)
+    cairn_b200.mma_unordered(m, n, k, ct, to_dev(fmt, a, dev), to_dev(fmt, b, dev))
+    cairn_b200.stream_status()
+    return ct.cpu().numpy()
+
+
+def within(got: np.ndarray, want: np.ndarray, tol: np.ndarray) -> np.ndarray:
+    return np.abs(got.astype(np.float64) - want.astype(np.float64)) <= tol.ravel()
+
+
+def test_the_reference_fixtures_within_twice_the_contract(cuda):
+    d = np.load(GOLDEN / "mma.npz")
+    keys = sorted({"/".join(k.split("/")[:3]) for k in d.files})
+    for key in keys:
+        fmt, _, shape = key.split("/")
+        m, n, k = map(int, shape.split("x"))
+        c, a, b, want = d[key + "/c"], d[key + "/a"], d[key + "/b"], d[key + "/want"]
+        got = device_mma(fmt, c, a, b, m, n, k, cuda)
+        if m * n == 0:
+            continue
+        ok = within(got, want, 2 * bound(fmt, c, a, b, m, n, k))
+        assert ok.all(), (key, np.argwhere(~ok)[:4].ravel(), got[~ok][:4], want[~ok][:4])
+
+
+@pytest.mark.parametrize("fmt", inputs.FORMATS)
+@pytest.mark.parametrize("shape", [(128, 256, 64), (129, 264, 72), (256, 512, 1024), (1, 8, 8), (257, 136, 520),
+                                   (300, 128, 8), (64, 1000, 200), (513, 392, 96)])
+def test_tensor_path_shapes_against_the_oracle(cuda, fmt, shape):
+    m, n, k = shape
+    c, a, b = inputs.mma_case(fmt, m, n, k, seed=hash(shape) % 1000)
+    want = restated.mma(fmt, c, a, b, m, n, k)
+    got = device_mma(fmt, c, a, b, m, n, k, cuda)
+    ok = within(got, want, 2 * bound(fmt, c, a, b, m, n, k))
+    assert ok.all(), (fmt, shape, np.argwhere(~ok)[:4].ravel())
+
+
+@pytest.mark.parametrize("shape", [(65, 63, 33), (3, 129, 31), (130, 70, 100), (7, 5, 3)])
+def test_shapes_off_the_tensor_map_rules_take_the_simt_tiles(cuda, shape):
+    """k or n not a multiple of 8 leaves rows off 16 bytes: the SIMT tile kernel computes the same contract."""
+    m, n, k = shape
+    for fmt in inputs.FORMATS:
+        c, a, b = inputs.tile_case(fmt, m, n, k)
+        want = restated.mma(fmt, c, a, b, m, n, k)
+        got = device_mma(fmt, c, a, b, m, n, k, cuda)
+        assert within(got, want, 2 * bound(fmt, c, a, b, m, n, k)).all(), (fmt, shape)
+
+
+def test_a_multiply_with_no_products_keeps_every_old_value(cuda):
+    c = np.asarray([-0.0, 1.5, -2.0, 3.0], np.float32)
+    got = device_mma("bf16", c, np.zeros(0, np.uint16), np.zeros(0, np.uint16), 2, 2, 0, cuda)
+    assert np.array_equal(got.view(np.uint32), c.view(np.uint32))
+
+
+def test_two_runs_give_the_same_bits(cuda):
+    m, n, k = 640, 768, 1024
+    c, a, b = inputs.mma_case("bf16", m, n, k, seed=5)
+    first = device_mma("bf16", c, a, b, m, n, k, cuda)
+    second = device_mma("bf16", c, a, b, m, n, k, cuda)
+    assert np.array_equal(first.view(np.uint32), second.view(np.uint32))
+
+
+@pytest.mark.parametrize("trans_a,trans_b", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("fmt", ["bf16", "f16"])
+def test_transposed_operands_of_the_backward(cuda, fmt, trans_a, trans_b):
+    """dX = dY * W^T (trans_b) and dW = X^T * dY (trans_a), as derive grad's loops form them."""
+    m, n, k = 200, 328, 136
+    rng = np.random.default_rng(17)
+    a = inputs.encode(fmt, rng.standard_normal(m * k))
+    b = inputs.encode(fmt, rng.standard_normal(k * n))
+    c = np.zeros(m * n, np.float32)
+    want = restated.gemm_t16(c, a, b, m, n, k, trans_a, trans_b, fmt)
+    at, bt = to_dev(fmt, a, cuda), to_dev(fmt, b, cuda)
+    at = at.view(k, m) if trans_a else at.view(m, k)
+    bt = bt.view(n, k) if trans_b else bt.view(k, n)
+    got = cairn_b200.gemm(at, bt, trans_a=trans_a, trans_b=trans_b).cpu().numpy().ravel()
+    cairn_b200.stream_status()
+    av = np.abs(inputs.decode(fmt, a)).reshape(k, m).T if trans_a else np.abs(inputs.decode(fmt, a)).reshape(m, k)
+    bv = np.abs(inputs.decode(fmt, b)).reshape(n, k).T if trans_b else np.abs(inputs.decode(fmt, b)).reshape(k, n)
+    tol = 2 * (k + 1) * 2.0**-22 * (av @ bv)
+    assert within(got, want, tol).all()
+
+
+def test_accumulate_and_store_epilogues(cuda):
+    m, n, k = 256, 256, 128
+    rng = np.random.default_rng(4)
+    a = inputs.encode("bf16", rng.standard_normal(m * k))
+    b = inputs.encode("bf16", rng.standard_normal(k * n))
+    c = rng.uniform(-4, 4, m * n).astype(np.float32)
+    at, bt = to_dev("bf16", a, cuda).view(m, k), to_dev("bf16", b, cuda).view(k, n)
+    out = torch.from_numpy(c.copy()).to(cuda).view(m, n)
+    cairn_b200.gemm(at, bt, out=out, accumulate=True)
+    stored = cairn_b200.gemm(at, bt)
+    cairn_b200.stream_status()
+    tol = 2 * bound("bf16", c, a, b, m, n, k)
+    assert within(out.cpu().numpy().ravel(), restated.mma("bf16", c, a, b, m, n, k), tol).all()
+    zero = np.zeros(m * n, np.float32)
+    assert within(stored.cpu().numpy().ravel(), restated.mma("bf16", zero, a, b, m, n, k), tol).all()
+
+
+def _bf16_close(got_bits: np.ndarray, want_bits: np.ndarray, acc_tol: np.ndarray) -> np.ndarray:
+    g, w = inputs.decode("bf16", got_bits), inputs.decode("bf16", want_bits)
+    return (np.abs(g - w) <= 2.0**-7 * np.maximum(np.abs(g), np.abs(w)) + acc_tol.ravel()) | (got_bits == want_bits)
+
+
+@pytest.mark.parametrize("relu", [True, False])
+def test_fused_bias_relu_bf16_epilogue(cuda, relu):
+    """bf16(act(acc + bias)): within one bf16 rounding of the oracle's epilogue on its own accumulator."""
+    m, n, k = 384, 520, 256
+    rng = np.random.default_rng(8)
+    a = inputs.encode("bf16", rng.standard_normal(m * k))
+    b = inputs.encode("bf16", rng.standard_normal(k * n))
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    acc = restated.mma("bf16", np.zeros(m * n, np.float32), a, b, m, n, k)
+    want = restated.bias_act(acc, bias, relu, m, n)
+    at, bt = to_dev("bf16", a, cuda).view(m, k), to_dev("bf16", b, cuda).view(k, n)
+    got = cairn_b200.gemm(at, bt, bias=torch.from_numpy(bias).to(cuda), relu=relu, out_dtype=torch.bfloat16)
+    cairn_b200.stream_status()
+    got_bits = got.view(torch.int16).cpu().numpy().view(np.uint16).ravel()
+    ok = _bf16_close(got_bits, want, 2 * bound("bf16", np.zeros(m * n, np.float32), a, b, m, n, k))
+    assert ok.all()
+    if relu:
+        assert (inputs.decode("bf16", got_bits) >= 0).all()
+
+
+def test_tf32_multiply_of_f32_operands(cuda):
+    m, n, k = 300, 264, 392
+    rng = np.random.default_rng(12)
+    a = rng.uniform(-1, 1, m * k).astype(np.float32)
+    b = rng.uniform(-1, 1, k * n).astype(np.float32)
+    c = rng.uniform(-4, 4, m * n).astype(np.float32)
+    want = restated.mma("f32", c, a, b, m, n, k)
+    ct = torch.from_numpy(c.copy()).to(cuda)
+    cairn_b200.mma_unordered(m, n, k, ct, torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda))
+    cairn_b200.stream_status()
+    mag = np.abs(c).reshape(m, n).astype(np.float64) + np.abs(a.reshape(m, k)).astype(np.float64) @ np.abs(
+        b.reshape(k, n)).astype(np.float64)
+    tol = (2.0**-9 + (k + 1) * 2.0**-22) * mag  # each operand rounded to tf32 (10 fraction bits), then f32 sums
+    assert within(ct.cpu().numpy(), want, tol).all()
+
+
+@pytest.mark.slow
+def test_baseline_4096_cubed_bias_relu_on_sampled_rows(cuda):
+    """4096^3 bf16, A, B ~ N(0,1) cast to bf16, bias ~ N(0, 0.1), ReLU, bf16 out. Sampled rows
+    against the oracle: Frobenius relative error within 2e-2 (the north star) and every element within one bf16
+    rounding plus twice the contract bound."""
+    m = n = k = 4096
+    g = torch.Generator(device=cuda).manual_seed(0)
+    a = torch.randn(m, k, device=cuda, generator=g).to(torch.bfloat16)
+    b = torch.randn(k, n, device=cuda, generator=g).to(torch.bfloat16)
+    bias = torch.randn(n, device=cuda, generator=g) * 0.1
+    out = cairn_b200.gemm(a, b, bias=bias, relu=True, out_dtype=torch.bfloat16)
+    cairn_b200.stream_status()
+    rows = [0, 1, 127, 128, 2047, 4095]
+    a_np = a.view(torch.int16).cpu().numpy().view(np.uint16).ravel()
+    b_np = b.view(torch.int16).cpu().numpy().view(np.uint16).ravel()
+    bias_np = bias.cpu().numpy()
+    for r in rows:
+        acc = restated.mma_bf16_rows(a_np, b_np, m, n, k, r, r + 1)
+        want = restated.bias_act(acc, bias_np, True, 1, n)
+        got = out[r].view(torch.int16).cpu().numpy().view(np.uint16)
+        gv, wv = inputs.decode("bf16", got), inputs.decode("bf16", want)
+        assert np.linalg.norm(gv - wv) <= 2e-2 * np.linalg.norm(wv), r
+        av = np.abs(inputs.decode("bf16", a_np[r * k:(r + 1) * k]))
+        tol = 2 * (k + 1) * 2.0**-22 * (av @ np.abs(inputs.decode("bf16", b_np).reshape(k, n)))
+        assert _bf16_close(got, want, tol).all(), r
