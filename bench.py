@@ -1,0 +1,561 @@
+#!/usr/bin/env python
+"""Benchmark of CAIRN's data-parallel hot path on B200, one JSON line per run (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm|saxpy|sum_f32|sum_u64|gemm5]
+                    [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...        (one rank per GPU, NCCL)
+
+Workloads (the default is the one the headline metric is quoted on):
+  gemm     config 2: bf16 GEMM M=N=K=4096, f32 accumulate, fused bias (N-vector ~ N(0, 0.1)) + ReLU, bf16 out.
+           One step = one product. At N GPUs each rank computes its own 4096-row block of an M = 4096 N product
+           with the same B (the M-sharded row-block partition, no collective): weak scaling.
+  gemm5    config 5: M-sharded bf16 GEMM, M = 65536, N = K = 8192, f32 out; rank r computes rows [r M/N, (r+1) M/N):
+           strong scaling (total work fixed).
+  saxpy    config 4: out = 2.5 x + y over n = 2^30 f32, range-sharded: strong scaling.
+  sum_f32  config 4: `reduce +` over n = 2^30 f32 (exact sum rounded once), range-sharded; the ranks' parts meet in
+           one NCCL all-gather and a combine kernel on every rank.
+  sum_u64  config 4: checked `reduce +` over n = 2^30 u64 (data[i] = i), range-sharded, parts all-gathered.
+Inputs are synthetic (seeded torch generators on the device), larger than L2 across the timed steps: every step
+reads a different buffer set, or (2^30 workloads) buffers far larger than the 126 MB L2.
+
+Timing: W untimed steps, then exactly K steps between a barrier and a device synchronize, timed with CUDA events on
+the launching stream; the max over ranks is reported. `value` is whole-job throughput with inputs resident in HBM;
+`e2e` is the same metric through the C ABI from pinned host buffers with the copies inside the timed region;
+`roofline` divides the dominant kernel's algorithmic work per launch by its event-timed launch duration and by the
+measured peak (MEASURED_PEAKS.json); `cpu_baseline` times the reference's own host path (the CAIRN runtime's
+lane-pool code, compiled from its sources into oracle/_ref) on a bounded sample on this box's cores.
+`--impl reference` runs only that CPU path, as the reference arm.
+"""
+
+from __future__ import annotations
+
+import argparse
+import ctypes as C
+import datetime
+import json
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+BASELINE_METRIC = "bf16 GEMM TFLOP/s & % tensor peak; reduce/saxpy HBM GB/s at 1/2/4/8 B200"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# plumbing
+# ---------------------------------------------------------------------------------------------------------------------
+class Dist:
+    def __init__(self, gpus: int):
+        import torch
+        import torch.distributed as dist
+
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local = int(os.environ.get("LOCAL_RANK", "0"))
+        if self.world != gpus:
+            raise SystemExit(f"--gpus {gpus} but WORLD_SIZE={self.world}: launch N>1 with torchrun")
+        self.dist = dist
+        self.device = torch.device("cuda", self.local) if torch.cuda.is_available() else None
+        if self.device is not None:
+            torch.cuda.set_device(self.device)
+        if self.world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=self.device)
+
+    def barrier(self):
+        if self.world > 1:
+            self.dist.barrier()
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        import torch
+
+        t = torch.tensor([x], dtype=torch.float64, device=self.device)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1:
+            self.dist.destroy_process_group()
+
+
+def measured_peaks() -> tuple[dict, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        return json.loads(path.read_text()), "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def profile_traffic(name: str) -> int | None:
+    """Per-launch DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) recorded from an ncu capture in
+    profiles/<name>.md as `traffic_per_launch_bytes: N`."""
+    path = ROOT / "profiles" / f"{name}.md"
+    if not path.exists():
+        return None
+    m = re.search(r"traffic_per_launch_bytes:\s*(\d+)", path.read_text())
+    return int(m.group(1)) if m else None
+
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons every 100 ms; `window` keeps those inside [t0, t1]."""
+
+    QUERY = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.samples: list[tuple[float, list[str]]] = []
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-i", str(index),
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) == 6:
+                self.samples.append((time.time(), parts))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def window(self, t0: float, t1: float) -> dict:
+        inside = [s for t, s in self.samples if t0 <= t <= t1]
+        note = None
+        if not inside and self.samples:  # a timed region shorter than the sampling period: the nearest samples
+            nearest = sorted(self.samples, key=lambda ts: min(abs(ts[0] - t0), abs(ts[0] - t1)))[:3]
+            inside = [s for _, s in nearest]
+            note = "timed region shorter than the 100 ms sampling period: nearest samples of the same run"
+        if not inside:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for s in inside for i in range(4) if s[2 + i].lower().startswith("active")})
+        out = {"sm_mhz": statistics.median(float(s[0]) for s in inside), "sm_max_mhz": float(inside[0][1]),
+               "reasons": reasons, "samples": len(inside)}
+        if note:
+            out["note"] = note
+        return out
+
+
+def time_steps(dist: Dist, stream, launch, steps: int, warmup: int, per_launch: bool = True):
+    """W warm-up steps, then K steps timed on `stream` with CUDA events (a barrier and a synchronize on both
+    sides). Returns (max-over-ranks ms per step, mean per-launch ms on this rank, wall t0, wall t1)."""
+    import torch
+
+    for i in range(warmup):
+        launch(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    marks = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)] \
+        if per_launch else []
+    t0 = time.time()
+    start.record(stream)
+    for i in range(steps):
+        if per_launch:
+            marks[i][0].record(stream)
+        launch(warmup + i)
+        if per_launch:
+            marks[i][1].record(stream)
+    end.record(stream)
+    torch.cuda.synchronize()
+    t1 = time.time()
+    dist.barrier()
+    total = start.elapsed_time(end)
+    launch_ms = statistics.fmean(a.elapsed_time(b) for a, b in marks) if per_launch else total / steps
+    return dist.max(total) / steps, launch_ms, t0, t1
+
+
+def lib_handle():
+    import cairn_b200
+
+    return cairn_b200.lib()
+
+
+def check(status: int, what: str):
+    if status != 0:
+        raise SystemExit(f"{what} failed with status {status}")
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# CPU baseline: the reference's own host path (oracle/_ref), or the C restatement when it was not built
+# ---------------------------------------------------------------------------------------------------------------------
+def cpu_kind():
+    from oracle import reference
+
+    return "reference" if reference.available() else "port"
+
+
+def cpu_gemm_sample(m_total: int, n: int, k: int, budget_s: float):
+    """TFLOP/s of the host multiply (cr::tensor::reference on the reference's lane pool, one lane per row of c) plus
+    the bias/ReLU/bf16 epilogue, on a sample of rows sized to take about `budget_s`."""
+    import numpy as np
+
+    from oracle import reference, restated
+
+    rng = np.random.default_rng(0)
+    b = rng.integers(0, 1 << 16, k * n, dtype=np.uint16) & np.uint16(0xBFFF)  # finite bf16 patterns
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    kind = cpu_kind()
+    rows, spent, flops = 4, 0.0, 0.0
+    while spent < budget_s:
+        a = rng.integers(0, 1 << 16, rows * k, dtype=np.uint16) & np.uint16(0xBFFF)
+        c = np.zeros(rows * n, np.float32)
+        t = time.perf_counter()
+        if kind == "reference":
+            acc = reference.mma_bf16_pooled(c, a, b, rows, n, k)
+        else:
+            acc = restated.mma("bf16", c, a, b, rows, n, k)
+        restated.bias_act(acc, bias, True, rows, n)
+        spent += time.perf_counter() - t
+        flops += 2.0 * rows * n * k
+        rows = min(rows * 2, m_total)
+    cores = reference.lanes() if kind == "reference" else 1
+    return flops / spent / 1e12, cores, kind, f"{int(flops / (2 * n * k))} rows of the {m_total}x{n}x{k} product"
+
+
+def cpu_stream_sample(workload: str, budget_s: float):
+    import numpy as np
+
+    from oracle import reference, restated
+
+    kind = cpu_kind()
+    n = 1 << 26
+    rng = np.random.default_rng(0)
+    x = rng.uniform(-1, 1, n).astype(np.float32)
+    y = rng.uniform(-1, 1, n).astype(np.float32)
+    u = np.arange(n, dtype=np.uint64)
+    out = np.empty_like(x)
+    lib = reference if kind == "reference" else restated
+    per = {"saxpy": 12, "sum_f32": 4, "sum_u64": 8}[workload]
+    spent, done = 0.0, 0
+    while spent < budget_s:
+        t = time.perf_counter()
+        if workload == "saxpy":
+            if kind == "reference":
+                reference.saxpy(2.5, x, y, out)
+            else:
+                restated.saxpy(2.5, x, y)
+        elif workload == "sum_f32":
+            lib.sum_f32(x)
+        else:
+            lib.sum_u64(u)
+        spent += time.perf_counter() - t
+        done += n
+    cores = reference.lanes() if kind == "reference" else 1
+    return done * per / spent / 1e9, cores, kind, f"{done // n} passes over 2^26 elements"
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------------------------------------------------
+class Gemm:
+    """bf16 GEMM with the fused bias + ReLU + bf16 epilogue (config 2), or the M-sharded f32-out product (config 5)."""
+
+    def __init__(self, dist: Dist, config5: bool):
+        import torch
+
+        self.torch, self.dist, self.config5 = torch, dist, config5
+        if config5:
+            self.m_total, self.n, self.k = 65536, 8192, 8192
+            self.m = self.m_total // dist.world
+            self.scaling = "strong"
+        else:
+            self.m, self.n, self.k = 4096, 4096, 4096
+            self.m_total = self.m * dist.world
+            self.scaling = "weak"
+        dev = dist.device
+        row0 = dist.rank * self.m
+        # Enough buffer sets that consecutive steps never find their operands in the 126 MB L2.
+        per_set = (self.m * self.k + self.k * self.n) * 2 + self.m * self.n * (4 if config5 else 2)
+        self.sets = max(2, -(-3 * 126 * 2**20 // per_set))
+        gb = torch.Generator(device=dev).manual_seed(0)
+        b_std = 0.02 if config5 else 1.0
+        self.a, self.b, self.out = [], [], []
+        for s in range(self.sets):
+            ga = torch.Generator(device=dev).manual_seed(1_000_003 * (s + 1) + row0)
+            self.a.append(torch.randn(self.m, self.k, device=dev, generator=ga).to(torch.bfloat16))
+            self.b.append((torch.randn(self.k, self.n, device=dev, generator=gb) * b_std).to(torch.bfloat16))
+            self.out.append(torch.empty(self.m, self.n, device=dev,
+                                        dtype=torch.float32 if config5 else torch.bfloat16))
+        self.bias = (torch.randn(self.n, device=dev, generator=gb) * 0.1).float()
+        self.lib = lib_handle()
+        self.stream = torch.cuda.current_stream(dev)
+        self.flops = 2.0 * self.m * self.n * self.k
+
+    def launch(self, i: int):
+        s = i % self.sets
+        if self.config5:
+            st = self.lib.cairn_b200_gemm(self.stream.cuda_stream, 0, self.m, self.n, self.k, self.a[s].data_ptr(), 0,
+                                          self.b[s].data_ptr(), 0, self.out[s].data_ptr(), 1, None, 0)
+        else:
+            st = self.lib.cairn_b200_gemm(self.stream.cuda_stream, 0, self.m, self.n, self.k, self.a[s].data_ptr(), 0,
+                                          self.b[s].data_ptr(), 0, self.out[s].data_ptr(), 2, self.bias.data_ptr(), 1)
+        if st:
+            raise SystemExit(f"cairn_b200_gemm failed with status {st}")
+
+    def e2e(self, steps: int, warmup: int):
+        """The same product through the C ABI from pinned host memory: A, B and bias copied in, the bf16 (or f32)
+        result copied out, every step."""
+        torch = self.torch
+        a_h = [self.a[s].cpu().pin_memory() for s in range(2)]
+        b_h = self.b[0].cpu().pin_memory()
+        bias_h = self.bias.cpu().pin_memory()
+        out_h = torch.empty(self.out[0].shape, dtype=self.out[0].dtype).pin_memory()
+        a_d, b_d, bias_d, out_d = self.a[0], self.b[0], self.bias, self.out[0]
+        lib, st = self.lib, self.stream.cuda_stream
+        kind, bias_p, act = (1, None, 0) if self.config5 else (2, bias_d.data_ptr(), 1)
+
+        def step(i):
+            a_d.copy_(a_h[i % 2], non_blocking=True)
+            b_d.copy_(b_h, non_blocking=True)
+            bias_d.copy_(bias_h, non_blocking=True)
+            check(lib.cairn_b200_gemm(st, 0, self.m, self.n, self.k, a_d.data_ptr(), 0, b_d.data_ptr(), 0,
+                                      out_d.data_ptr(), kind, bias_p, act), "gemm")
+            out_h.copy_(out_d, non_blocking=True)
+
+        ms, _, _, _ = time_steps(self.dist, self.stream, step, steps, warmup, per_launch=False)
+        h2d = a_h[0].numel() * 2 + b_h.numel() * 2 + bias_h.numel() * 4
+        d2h = out_h.numel() * out_h.element_size()
+        return self.dist.world * self.flops / (ms * 1e-3) / 1e12, h2d, d2h
+
+
+class Stream:
+    """saxpy and the two `reduce +` collectors over n = 2^30 elements, range-sharded across the ranks."""
+
+    def __init__(self, dist: Dist, workload: str):
+        import torch
+
+        self.torch, self.dist, self.workload = torch, dist, workload
+        self.n_total = 1 << 30
+        lo = self.n_total * dist.rank // dist.world
+        hi = self.n_total * (dist.rank + 1) // dist.world
+        self.n = hi - lo
+        dev = dist.device
+        g = torch.Generator(device=dev).manual_seed(0 + dist.rank)
+        self.lib = lib_handle()
+        self.stream = torch.cuda.current_stream(dev)
+        if workload == "saxpy":
+            self.x = torch.rand(self.n, device=dev, generator=g) * 2 - 1
+            self.y = torch.rand(self.n, device=dev, generator=g) * 2 - 1
+            self.o = torch.empty_like(self.x)
+            self.bytes = 12
+        elif workload == "sum_f32":
+            self.x = torch.rand(self.n, device=dev, generator=g) * 2 - 1
+            self.part = torch.zeros(3, dtype=torch.float64, device=dev)
+            self.parts = torch.zeros(dist.world, 3, dtype=torch.float64, device=dev)
+            self.total = torch.zeros(1, dtype=torch.float32, device=dev)
+            self.bytes = 4
+        else:
+            self.x = torch.arange(lo, hi, device=dev, dtype=torch.int64).view(torch.uint64)
+            self.cell = torch.zeros(1, dtype=torch.int64, device=dev)
+            self.flag = torch.zeros(1, dtype=torch.int32, device=dev)
+            self.cells = torch.zeros(dist.world, dtype=torch.int64, device=dev)
+            self.flags = torch.zeros(dist.world, dtype=torch.int32, device=dev)
+            self.bytes = 8
+
+    def launch(self, i: int):
+        lib, st, dist = self.lib, self.stream.cuda_stream, self.dist
+        if self.workload == "saxpy":
+            check(lib.cairn_b200_saxpy_f32(st, self.n, self.o.data_ptr(), self.x.data_ptr(), self.y.data_ptr(), 2.5),
+                  "saxpy")
+        elif self.workload == "sum_f32":
+            if dist.world == 1:
+                check(lib.cairn_b200_sum_f32(st, self.n, self.x.data_ptr(), self.total.data_ptr()), "sum")
+            else:
+                check(lib.cairn_b200_sum_f32_partial(st, self.n, self.x.data_ptr(), self.part.data_ptr()), "sum")
+                dist.dist.all_gather_into_tensor(self.parts, self.part)
+                check(lib.cairn_b200_sum_f32_combine_device(st, self.parts.data_ptr(), dist.world,
+                                                            self.total.data_ptr()), "combine")
+        else:
+            check(lib.cairn_b200_sum_u64(st, self.n, self.x.data_ptr(), self.cell.data_ptr(), self.flag.data_ptr()),
+                  "sum_u64")
+            if dist.world > 1:
+                dist.dist.all_gather_into_tensor(self.cells, self.cell)
+                dist.dist.all_gather_into_tensor(self.flags, self.flag)
+
+    def e2e(self, steps: int, warmup: int):
+        torch = self.torch
+        lib, st = self.lib, self.stream.cuda_stream
+        chunk = min(self.n, 1 << 26)  # the e2e sample: 2^26 elements per rank from pinned host memory
+        x_h = self.x[:chunk].cpu().pin_memory()
+        x_d = self.x[:chunk]
+        if self.workload == "saxpy":
+            y_h, o_h = self.y[:chunk].cpu().pin_memory(), torch.empty(chunk, dtype=torch.float32).pin_memory()
+            y_d, o_d = self.y[:chunk], self.o[:chunk]
+
+            def step(i):
+                x_d.copy_(x_h, non_blocking=True)
+                y_d.copy_(y_h, non_blocking=True)
+                check(lib.cairn_b200_saxpy_f32(st, chunk, o_d.data_ptr(), x_d.data_ptr(), y_d.data_ptr(), 2.5), "saxpy")
+                o_h.copy_(o_d, non_blocking=True)
+
+            h2d, d2h = 8 * chunk, 4 * chunk
+        else:
+            res = torch.empty(1, dtype=torch.int64).pin_memory()
+            cell = torch.zeros(1, dtype=torch.int64, device=self.dist.device)
+            flag = torch.zeros(1, dtype=torch.int32, device=self.dist.device)
+
+            def step(i):
+                x_d.copy_(x_h, non_blocking=True)
+                if self.workload == "sum_f32":
+                    check(lib.cairn_b200_sum_f32(st, chunk, x_d.data_ptr(), cell.data_ptr()), "sum")
+                else:
+                    check(lib.cairn_b200_sum_u64(st, chunk, x_d.data_ptr(), cell.data_ptr(), flag.data_ptr()), "sum")
+                res.copy_(cell, non_blocking=True)
+
+            h2d, d2h = x_h.numel() * x_h.element_size(), 8
+        ms, _, _, _ = time_steps(self.dist, self.stream, step, steps, warmup, per_launch=False)
+        return self.dist.world * chunk * self.bytes / (ms * 1e-3) / 1e9, h2d, d2h
+
+
+# ---------------------------------------------------------------------------------------------------------------------
+def reference_arm(args, dist: Dist) -> None:
+    """The reference's own CPU implementation of the path (the CAIRN runtime's host code, oracle/_ref) on this box's
+    host cores, rank 0 only, each step a bounded sample of the workload."""
+    if dist.rank != 0:
+        return
+    from oracle import reference
+
+    budget = max(0.2, min(5.0, 90.0 / max(1, args.steps + args.warmup)))
+    if args.workload in ("gemm", "gemm5"):
+        m, n, k = (4096, 4096, 4096) if args.workload == "gemm" else (65536, 8192, 8192)
+        for _ in range(args.warmup):
+            cpu_gemm_sample(m, n, k, budget / 4)
+        vals = [cpu_gemm_sample(m, n, k, budget) for _ in range(args.steps)]
+        unit, sample = "TFLOP/s", vals[-1][3]
+    else:
+        for _ in range(args.warmup):
+            cpu_stream_sample(args.workload, budget / 4)
+        vals = [cpu_stream_sample(args.workload, budget) for _ in range(args.steps)]
+        unit, sample = "GB/s", vals[-1][3]
+    value = statistics.median(v[0] for v in vals)
+    cores, kind = vals[-1][1], vals[-1][2]
+    line = {"metric": BASELINE_METRIC, "value": value, "unit": unit, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
+            "scaling": "weak" if args.workload == "gemm" else "strong", "vs_baseline": None,
+            "dtype": "bf16" if args.workload.startswith("gemm") else ("f32" if args.workload != "sum_u64" else "u64"),
+            "data": "synthetic", "config": config_of(args, dist),
+            "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind,
+                             "sample": f"per step: {sample}"},
+            "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if not reference.available():
+        line["note"] = "oracle/_ref not built on this box: the C restatement of the reference's host path ran"
+    print(json.dumps(line), flush=True)
+
+
+def config_of(args, dist: Dist) -> dict:
+    w = args.workload
+    if w == "gemm":
+        return {"workload": "config 2: bf16 GEMM 4096^3, fused bias + ReLU, bf16 out", "m": 4096 * dist.world,
+                "n": 4096, "k": 4096, "rows_per_gpu": 4096, "parallelism": f"row-block x{dist.world}",
+                "l2": "inputs rotate over buffer sets larger than L2"}
+    if w == "gemm5":
+        return {"workload": "config 5: M-sharded bf16 GEMM, f32 out", "m": 65536, "n": 8192, "k": 8192,
+                "parallelism": f"row-block x{dist.world}", "l2": "inputs rotate over buffer sets larger than L2"}
+    return {"workload": f"config 4: {w} over n = 2^30", "n": 1 << 30, "parallelism": f"range x{dist.world}",
+            "l2": "inputs larger than L2"}
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--workload", default="gemm", choices=["gemm", "gemm5", "saxpy", "sum_f32", "sum_u64"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU-baseline leg")
+    args = ap.parse_args()
+    defaults = {"gemm": (2000, 50), "gemm5": (50, 5), "saxpy": (100, 5), "sum_f32": (200, 5), "sum_u64": (100, 5)}
+    d_steps, d_warm = defaults[args.workload] if args.impl == "ours" else (5, 1)
+    args.steps = args.steps if args.steps is not None else d_steps
+    args.warmup = args.warmup if args.warmup is not None else d_warm
+    if args.impl == "ours" and args.warmup < 3:
+        args.warmup = 3  # the contract's least warm-up
+
+    dist = Dist(args.gpus)
+    if args.impl == "reference":
+        reference_arm(args, dist)
+        dist.close()
+        return
+    import torch
+
+    wl = Gemm(dist, args.workload == "gemm5") if args.workload.startswith("gemm") else Stream(dist, args.workload)
+    peaks, peak_source = measured_peaks()
+    sampler = ClockSampler(dist.local)
+    ms, launch_ms, t0, t1 = time_steps(dist, wl.stream, wl.launch, args.steps, args.warmup)
+    clocks = sampler.window(t0, t1)
+    sampler.stop()
+    stat = lib_handle().cairn_b200_stream_status(wl.stream.cuda_stream)
+    if stat:
+        raise SystemExit(f"device status {stat} after the timed steps")
+    e2e_val, h2d, d2h = wl.e2e(max(3, min(args.steps, 20)), 3)
+
+    if isinstance(wl, Gemm):
+        value = dist.world * wl.flops / (ms * 1e-3) / 1e12
+        unit, bound, dtype = "TFLOP/s", "tensor", "bf16"
+        achieved = wl.flops / (launch_ms * 1e-3) / 1e12
+        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        kernel = "tc_gemm_kernel"
+        traffic = profile_traffic("gemm_bf16_4096_bias_relu" if args.workload == "gemm" else "gemm_bf16_config5")
+    else:
+        per_rank_bytes = wl.n * wl.bytes
+        value = dist.world * per_rank_bytes / (ms * 1e-3) / 1e9
+        unit, bound = "GB/s", "hbm"
+        dtype = {"saxpy": "f32", "sum_f32": "f32", "sum_u64": "u64"}[args.workload]
+        achieved = per_rank_bytes / (launch_ms * 1e-3) / 1e9
+        peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+        kernel = {"saxpy": "saxpy_vec_kernel", "sum_f32": "sum_f32_kernel", "sum_u64": "sum_u64_kernel"}[args.workload]
+        traffic = profile_traffic(f"{args.workload}_2p30")
+
+    cpu = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        if isinstance(wl, Gemm):
+            v, cores, kind, sample = cpu_gemm_sample(wl.m, wl.n, wl.k, 12.0)
+        else:
+            v, cores, kind, sample = cpu_stream_sample(args.workload, 12.0)
+        cpu = {"value": v, "unit": unit, "cores": cores, "kind": kind, "sample": sample}
+
+    launches = args.steps * (1 if isinstance(wl, Gemm) or args.workload != "sum_f32" or dist.world == 1 else 2)
+    line = {
+        "metric": BASELINE_METRIC, "value": value, "unit": unit, "n_gpus": dist.world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": wl.scaling
+        if isinstance(wl, Gemm) else "strong", "vs_baseline": None, "dtype": dtype,
+        "data": "synthetic (seeded device generators; random-init operands of the configs' shapes and distributions)",
+        "config": config_of(args, dist),
+        "roofline": {"bound": bound, "kernel": kernel, "achieved": achieved, "peak": peak, "unit": unit,
+                     "frac": achieved / peak, "peak_source": f"{peak_source} ({'bf16_tflops burst' if bound == 'tensor' else 'hbm_gbs'})",
+                     "traffic": traffic},
+        "cpu_baseline": cpu,
+        "clocks": clocks,
+        "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "gpu_launches": launches,
+    }
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+    del wl
+    torch.cuda.synchronize()
+    dist.close()
+
+
+if __name__ == "__main__":
+    main()

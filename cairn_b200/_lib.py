@@ -41,6 +41,7 @@ SIGNATURES: dict[str, tuple] = {
     "cairn_b200_sum_f32_partial": (_i, [_p, _z, _p, _p]),
     "cairn_b200_sum_f32_host": (_i, [_p, _z, _p, C.POINTER(C.c_float)]),
     "cairn_b200_sum_f32_combine": (_i, [_p, _z, C.POINTER(C.c_float)]),
+    "cairn_b200_sum_f32_combine_device": (_i, [_p, _p, _z, _p]),
     "cairn_b200_sum_u64": (_i, [_p, _z, _p, _p, _p]),
     "cairn_b200_sum_u64_host": (_i, [_p, _z, _p, C.POINTER(C.c_uint64), _ip]),
     "cairn_b200_stream_status": (_i, [_p]),

@@ -380,6 +380,14 @@ int cairn_b200_sum_f32_combine(const double* parts, size_t count, float* result)
   return CAIRN_B200_OK;
 }
 
+int cairn_b200_sum_f32_combine_device(void* stream, const double* parts, size_t count, float* out) {
+  if (!view_ok(parts, count * 3, 8, 8) || !view_ok(out, 1, 4, 4) || count > 1u << 20) return CAIRN_B200_ERR_VIEW;
+  int status;
+  const Device* d = current(&status);
+  if (!d) return status;
+  return cuda_status(combine_f32_parts_launch(parts, static_cast<int>(count), out, static_cast<cudaStream_t>(stream)));
+}
+
 int cairn_b200_stream_status(void* stream) {
   const cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return CAIRN_B200_ERR_CUDA;

@@ -250,6 +250,12 @@ __global__ void __launch_bounds__(192, 1)
       // Leading/stride byte offsets: a K-major tile is rows of 128 bytes, 8-row swizzle atoms 1024 bytes apart; an
       // M/N-major tile is CH-element chunks of SLICE rows each (chunk stride CH * SLICE bytes), 8 k rows per atom.
       const std::uint32_t a_lbo = p.a_mn ? CH * SLICE : 16u, b_lbo = p.b_k ? 16u : CH * SLICE;
+      // An M/N-major tf32 tile uses 4-row atoms (512 bytes apart); everything else 8-row atoms (1024 bytes apart).
+      constexpr bool MN32 = F::bytes == 4;
+      const std::uint32_t a_layout = (MN32 && p.a_mn) ? LAYOUT_SW128_32B : LAYOUT_SW128;
+      const std::uint32_t b_layout = (MN32 && !p.b_k) ? LAYOUT_SW128_32B : LAYOUT_SW128;
+      const std::uint32_t a_sbo = a_layout == LAYOUT_SW128_32B ? 512u : 1024u;
+      const std::uint32_t b_sbo = b_layout == LAYOUT_SW128_32B ? 512u : 1024u;
       std::uint32_t stage = 0, phase = 0, it = 0;
       for (int t = blockIdx.x; t < tiles; t += gridDim.x, ++it) {
         const std::uint32_t acc = it & 1u, acc_phase = (it >> 1) & 1u;
@@ -265,8 +271,8 @@ __global__ void __launch_bounds__(192, 1)
           for (int kk = 0; kk < SLICE / MMA_K_BYTES; ++kk) {
             const std::uint32_t a_off = p.a_mn ? kk * (MMA_K_ROWS / 8) * 1024 : kk * MMA_K_BYTES;
             const std::uint32_t b_off = p.b_k ? kk * MMA_K_BYTES : kk * (MMA_K_ROWS / 8) * 1024;
-            const std::uint64_t a_desc = sdesc_sw128(a_addr + a_off, a_lbo, 1024);
-            const std::uint64_t b_desc = sdesc_sw128(b_addr + b_off, b_lbo, 1024);
+            const std::uint64_t a_desc = sdesc(a_addr + a_off, a_lbo, a_sbo, a_layout);
+            const std::uint64_t b_desc = sdesc(b_addr + b_off, b_lbo, b_sbo, b_layout);
             umma<F::kind>(d_tmem, a_desc, b_desc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           tc_commit(&empty[stage]);
@@ -447,18 +453,20 @@ CUtensorMapDataType map_type(int fmt) {
   }
 }
 
-// A 2-D row-major array of `rows` rows of `cols` elements, read in boxes of box_cols x box_rows, 128-byte swizzled.
+// A 2-D row-major array of `rows` rows of `cols` elements, read in boxes of box_cols x box_rows with 128-byte rows,
+// swizzled as the MMA will read the tile: 32-byte atoms for an M/N-major 32-bit operand, 16-byte atoms otherwise.
 bool encode(CUtensorMap* map, int fmt, const void* base, std::uint64_t cols, std::uint64_t rows, int esize,
-            std::uint32_t box_cols, std::uint32_t box_rows) {
+            std::uint32_t box_cols, std::uint32_t box_rows, bool mn_major) {
   EncodeTiled fn = encoder();
   if (!fn) return false;
   const cuuint64_t dims[2] = {cols, rows};
   const cuuint64_t strides[1] = {cols * static_cast<cuuint64_t>(esize)};
   const cuuint32_t box[2] = {box_cols, box_rows};
   const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapSwizzle swizzle =
+      (mn_major && esize == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
   return fn(map, map_type(fmt), 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 int esize_of(int fmt) { return fmt == FMT_TF32 ? 4 : (fmt == FMT_E4M3 || fmt == FMT_E5M2) ? 1 : 2; }
@@ -471,8 +479,10 @@ cudaError_t launch_tc(const GemmArgs& g, const TcParams& p, cudaStream_t stream,
   constexpr int CH = SLICE / Fmt<FMT>::bytes;
   const int es = Fmt<FMT>::bytes;
   CUtensorMap ta, tb;
-  const bool ok_a = g.trans_a ? encode(&ta, FMT, g.a, g.m, g.k, es, CH, CH) : encode(&ta, FMT, g.a, g.k, g.m, es, CH, BM);
-  const bool ok_b = g.trans_b ? encode(&tb, FMT, g.b, g.k, g.n, es, CH, BN) : encode(&tb, FMT, g.b, g.n, g.k, es, CH, CH);
+  const bool ok_a = g.trans_a ? encode(&ta, FMT, g.a, g.m, g.k, es, CH, CH, true)
+                              : encode(&ta, FMT, g.a, g.k, g.m, es, CH, BM, false);
+  const bool ok_b = g.trans_b ? encode(&tb, FMT, g.b, g.k, g.n, es, CH, BN, false)
+                              : encode(&tb, FMT, g.b, g.n, g.k, es, CH, CH, true);
   if (!ok_a || !ok_b) return cudaErrorInvalidValue;
   // The shared-memory opt-in is a property of the kernel on each device: set once per device before its first launch.
   static std::atomic<std::uint64_t> configured{0};

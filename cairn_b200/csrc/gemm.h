@@ -38,6 +38,7 @@ cudaError_t saxpy_f32_launch(std::size_t n, float* out, const float* x, const fl
                              int sms);
 cudaError_t sum_f32_launch(std::size_t n, const float* x, float* out_f32, double* out_f64, void* scratch,
                            cudaStream_t s, int sms);
+cudaError_t combine_f32_parts_launch(const double* parts, int count, float* out, cudaStream_t s);
 cudaError_t sum_u64_launch(std::size_t n, const std::uint64_t* x, std::uint64_t* out, std::uint32_t* overflow,
                            void* scratch, cudaStream_t s, int sms);
 

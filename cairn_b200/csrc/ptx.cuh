@@ -166,17 +166,21 @@ __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.
 // ---------------------------------------------------------------------------------------------------------------
 // UMMA descriptors (the sm_100 shared-memory matrix descriptor and the kind::f16/tf32/f8f6f4 instruction descriptor)
 // ---------------------------------------------------------------------------------------------------------------
-// Shared-memory matrix descriptor for a 128-byte-swizzled tile: start address, leading- and stride-dimension byte
-// offsets (all in 16-byte units), version 1 (sm_100) at bit 46, swizzle mode 2 (128B) at bits 61-63. The tile's
-// swizzle atoms (8 rows x 128 bytes) start on 1024-byte boundaries, so the base-offset field stays 0.
-__device__ __forceinline__ std::uint64_t sdesc_sw128(std::uint32_t saddr, std::uint32_t lbo_bytes,
-                                                     std::uint32_t sbo_bytes) {
+// Shared-memory layouts of the operand tiles: 128-byte rows, swizzled in 16-byte units over 8-row atoms (SW128), or
+// in 32-byte units over 4-row atoms (SW128_32B: the one layout UMMA reads an M/N-major 32-bit operand from).
+enum SmemLayout : std::uint32_t { LAYOUT_SW128 = 2, LAYOUT_SW128_32B = 1 };
+
+// Shared-memory matrix descriptor: start address, leading- and stride-dimension byte offsets (all in 16-byte
+// units), version 1 (sm_100) at bit 46, layout type at bits 61-63. Every tile starts on a 1024-byte boundary, a
+// whole number of swizzle atoms, so the base-offset field stays 0.
+__device__ __forceinline__ std::uint64_t sdesc(std::uint32_t saddr, std::uint32_t lbo_bytes, std::uint32_t sbo_bytes,
+                                               std::uint32_t layout) {
   std::uint64_t d = 0;
   d |= static_cast<std::uint64_t>((saddr >> 4) & 0x3fffu);
   d |= static_cast<std::uint64_t>((lbo_bytes >> 4) & 0x3fffu) << 16;
   d |= static_cast<std::uint64_t>((sbo_bytes >> 4) & 0x3fffu) << 32;
   d |= 1ull << 46;
-  d |= 2ull << 61;
+  d |= static_cast<std::uint64_t>(layout) << 61;
   return d;
 }
 

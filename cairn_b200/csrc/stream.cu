@@ -244,6 +244,28 @@ __global__ void __launch_bounds__(T, 2) sum_f32_kernel(std::size_t n, const floa
   }
 }
 
+// The sharded sum's last step, on the device: the ranks' parts (hi, lo, flags; cairn_b200_sum_f32_partial) added as
+// double-doubles in rank order and rounded once, as the single-device kernel rounds its blocks' total.
+__global__ void combine_f32_parts_kernel(const double* parts, int count, float* out) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  DD t{-0.0, -0.0};
+  unsigned tf = 0;
+  for (int p = 0; p < count; ++p) {
+    t = dd_add(t, DD{parts[3 * p], parts[3 * p + 1]});
+    tf |= static_cast<unsigned>(parts[3 * p + 2]);
+  }
+  const double hi = __dadd_rn(t.s, t.c);
+  const double z = __dsub_rn(hi, t.s);
+  const double lo = __dadd_rn(__dsub_rn(t.s, __dsub_rn(hi, z)), __dsub_rn(t.c, z));
+  float r;
+  if ((tf & SUM_NAN) || ((tf & SUM_PINF) && (tf & SUM_NINF))) r = __uint_as_float(0x7fc00000u);
+  else if (tf & SUM_PINF) r = __uint_as_float(0x7f800000u);
+  else if (tf & SUM_NINF) r = __uint_as_float(0xff800000u);
+  else if (hi == 0.0) r = ((tf & SUM_SOME) && !(tf & SUM_OTHER)) ? -0.0f : 0.0f;
+  else r = round_dd_f32(hi, lo);
+  *out = r;
+}
+
 // ---- u64 checked sum --------------------------------------------------------------------------------------------
 struct SumU64 {
   unsigned long long v;
@@ -363,6 +385,11 @@ cudaError_t sum_f32_launch(std::size_t n, const float* x, float* out_f32, double
   unsigned int* ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(scratch) + static_cast<std::size_t>(grid) * 32);
   if (aligned16(x)) sum_f32_kernel<true><<<grid, T, 0, s>>>(n, x, out_f32, out_f64, partials, ticket);
   else sum_f32_kernel<false><<<grid, T, 0, s>>>(n, x, out_f32, out_f64, partials, ticket);
+  return cudaGetLastError();
+}
+
+cudaError_t combine_f32_parts_launch(const double* parts, int count, float* out, cudaStream_t s) {
+  combine_f32_parts_kernel<<<1, 32, 0, s>>>(parts, count, out);
   return cudaGetLastError();
 }
 

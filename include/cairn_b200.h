@@ -102,11 +102,14 @@ int cairn_b200_saxpy_f32(void* stream, size_t n, float* out, const float* x, con
  *                 part of a sharded sum
  *   _f32_host     writes the total to *result in host memory and waits for the stream (the reduce_on form)
  *   _f32_combine  host only: the f32 total of `count` parts (3 doubles each, host memory), added exactly and rounded
- *                 once, as the host's cr::par::sum rounds the exact total of all the ranks' terms */
+ *                 once, as the host's cr::par::sum rounds the exact total of all the ranks' terms
+ *   _f32_combine_device  the same on `stream` from parts in device memory (after an all-gather of the ranks' parts),
+ *                 the parts added as double-doubles in rank order; the total lands in *out, a device f32 */
 int cairn_b200_sum_f32(void* stream, size_t n, const float* x, float* out);
 int cairn_b200_sum_f32_partial(void* stream, size_t n, const float* x, double* out);
 int cairn_b200_sum_f32_host(void* stream, size_t n, const float* x, float* result);
 int cairn_b200_sum_f32_combine(const double* parts, size_t count, float* result);
+int cairn_b200_sum_f32_combine_device(void* stream, const double* parts, size_t count, float* out);
 
 /* `reduce + parallel` over u64 with the checked sum cr::Sum<u64> (runtime/cairn_runtime.hpp:158-166): the total
  * modulo 2^64 and a sticky overflow flag that is 1 exactly when the true total does not fit. *out and *overflow are

@@ -203,3 +203,20 @@ def test_baseline_4096_cubed_bias_relu_on_sampled_rows(cuda):
         av = np.abs(inputs.decode("bf16", a_np[r * k:(r + 1) * k]))
         tol = 2 * (k + 1) * 2.0**-22 * (av @ np.abs(inputs.decode("bf16", b_np).reshape(k, n)))
         assert _bf16_close(got, want, tol).all(), r
+
+
+@pytest.mark.parametrize("trans_a,trans_b", [(False, False), (False, True), (True, False), (True, True)])
+def test_tf32_every_operand_layout(cuda, trans_a, trans_b):
+    """An M/N-major 32-bit operand needs the 32-byte-atom swizzle (SW128_32B); both layouts are held to f64 within
+    the tf32 bound."""
+    m, n, k = 264, 392, 200
+    rng = np.random.default_rng(31)
+    a = rng.uniform(-1, 1, (m, k)).astype(np.float32)
+    b = rng.uniform(-1, 1, (k, n)).astype(np.float32)
+    at = torch.from_numpy(np.ascontiguousarray(a.T) if trans_a else a).to(cuda)
+    bt = torch.from_numpy(np.ascontiguousarray(b.T) if trans_b else b).to(cuda)
+    got = cairn_b200.gemm(at, bt, trans_a=trans_a, trans_b=trans_b).cpu().numpy()
+    cairn_b200.stream_status()
+    want = a.astype(np.float64) @ b.astype(np.float64)
+    tol = (2.0**-9 + (k + 1) * 2.0**-22) * (np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64))
+    assert (np.abs(got - want) <= tol).all()
