@@ -342,11 +342,11 @@ class Gemm:
 class Stream:
     """saxpy and the two `reduce +` collectors over n = 2^30 elements, range-sharded across the ranks."""
 
-    def __init__(self, dist: Dist, workload: str):
+    def __init__(self, dist: Dist, workload: str, log2n: int = 30):
         import torch
 
         self.torch, self.dist, self.workload = torch, dist, workload
-        self.n_total = 1 << 30
+        self.n_total = 1 << log2n
         lo = self.n_total * dist.rank // dist.world
         hi = self.n_total * (dist.rank + 1) // dist.world
         self.n = hi - lo
@@ -472,8 +472,8 @@ def config_of(args, dist: Dist) -> dict:
     if w == "gemm5":
         return {"workload": "config 5: M-sharded bf16 GEMM, f32 out", "m": 65536, "n": 8192, "k": 8192,
                 "parallelism": f"row-block x{dist.world}", "l2": "inputs rotate over buffer sets larger than L2"}
-    return {"workload": f"config 4: {w} over n = 2^30", "n": 1 << 30, "parallelism": f"range x{dist.world}",
-            "l2": "inputs larger than L2"}
+    return {"workload": f"config 4: {w} over n = 2^{args.log2n}", "n": 1 << args.log2n,
+            "parallelism": f"range x{dist.world}", "l2": "inputs larger than L2"}
 
 
 def main() -> None:
@@ -484,6 +484,7 @@ def main() -> None:
     ap.add_argument("--workload", default="gemm", choices=["gemm", "gemm5", "saxpy", "sum_f32", "sum_u64"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU-baseline leg")
+    ap.add_argument("--log2n", type=int, default=30, help="saxpy/sum size 2^log2n (BASELINE: 30; smaller for ncu)")
     args = ap.parse_args()
     defaults = {"gemm": (2000, 50), "gemm5": (50, 5), "saxpy": (100, 5), "sum_f32": (200, 5), "sum_u64": (100, 5)}
     d_steps, d_warm = defaults[args.workload] if args.impl == "ours" else (5, 1)
@@ -499,7 +500,8 @@ def main() -> None:
         return
     import torch
 
-    wl = Gemm(dist, args.workload == "gemm5") if args.workload.startswith("gemm") else Stream(dist, args.workload)
+    wl = Gemm(dist, args.workload == "gemm5") if args.workload.startswith("gemm") else \
+        Stream(dist, args.workload, args.log2n)
     peaks, peak_source = measured_peaks()
     sampler = ClockSampler(dist.local)
     ms, launch_ms, t0, t1 = time_steps(dist, wl.stream, wl.launch, args.steps, args.warmup)

@@ -13,7 +13,7 @@ HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libcairn_b200.so"
 HEADER = HERE.parent / "include" / "cairn_b200.h"
 
-OK, ERR_SHAPE, ERR_VIEW, ERR_OVERLAP, ERR_OVERFLOW, ERR_CUDA, ERR_TIMEOUT, ERR_ARG, ERR_DEVICE = range(9)
+OK, ERR_SHAPE, ERR_VIEW, ERR_OVERLAP, ERR_OVERFLOW, ERR_CUDA, ERR_TIMEOUT, ERR_ARG, ERR_DEVICE, ERR_SCRATCH = range(10)
 BF16, F16, F8E4M3, F8E5M2, TF32 = range(5)
 OUT_ACC_F32, OUT_STORE_F32, OUT_BF16 = range(3)
 ACT_NONE, ACT_RELU = range(2)
@@ -42,6 +42,7 @@ SIGNATURES: dict[str, tuple] = {
     "cairn_b200_sum_f32_host": (_i, [_p, _z, _p, C.POINTER(C.c_float)]),
     "cairn_b200_sum_f32_combine": (_i, [_p, _z, C.POINTER(C.c_float)]),
     "cairn_b200_sum_f32_combine_device": (_i, [_p, _p, _z, _p]),
+    "cairn_b200_sum_f32_noalloc": (_i, [_p, _z, _p, _p]),
     "cairn_b200_sum_u64": (_i, [_p, _z, _p, _p, _p]),
     "cairn_b200_sum_u64_host": (_i, [_p, _z, _p, C.POINTER(C.c_uint64), _ip]),
     "cairn_b200_stream_status": (_i, [_p]),

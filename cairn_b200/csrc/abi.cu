@@ -405,6 +405,7 @@ const char* cairn_b200_status_string(int status) {
     case CAIRN_B200_ERR_TIMEOUT: return "a device-side wait ran out its bound";
     case CAIRN_B200_ERR_ARG: return "an argument is outside the entry's domain";
     case CAIRN_B200_ERR_DEVICE: return "the current device is not an sm_100 part";
+    case CAIRN_B200_ERR_SCRATCH: return "the launch needs more partial cells than the static scratch array holds";
     default: return "unknown status";
   }
 }

@@ -32,7 +32,8 @@ enum cairn_b200_status {
   CAIRN_B200_ERR_CUDA = 5,     /* a CUDA call failed: cr::gpu::check aborts, runtime/cairn_kernels.hpp:55-59 */
   CAIRN_B200_ERR_TIMEOUT = 6,  /* a device-side wait ran out its bound (no reference counterpart: it traps nowhere) */
   CAIRN_B200_ERR_ARG = 7,      /* an argument outside the entry's domain (unknown format, activation, ...) */
-  CAIRN_B200_ERR_DEVICE = 8    /* no sm_100 device is current */
+  CAIRN_B200_ERR_DEVICE = 8,   /* no sm_100 device is current */
+  CAIRN_B200_ERR_SCRATCH = 9   /* the launch needs more than a fixed scratch array holds (cairn_b200_sum_f32_noalloc) */
 };
 
 /* Storage formats of the multiply's operands (runtime/cairn_float.hpp:160-167), and f32 read as tf32. */
@@ -117,6 +118,17 @@ int cairn_b200_sum_f32_combine_device(void* stream, const double* parts, size_t 
  * .checked() would trap, with the wrapped total still written. */
 int cairn_b200_sum_u64(void* stream, size_t n, const uint64_t* x, uint64_t* out, uint32_t* overflow);
 int cairn_b200_sum_u64_host(void* stream, size_t n, const uint64_t* x, uint64_t* result, int* overflow);
+
+/* The f32 sum of cairn_b200_sum_f32 for callers that cannot allocate device memory: no reference counterpart (the
+ * reference's reductions always take their temporaries from the context's arena). A serving process whose device
+ * memory is reserved up front by its own allocator, or a loop that cannot afford a cudaMalloc's implicit
+ * synchronization, calls this form: it runs the same kernel over a scratch array compiled into the library
+ * (32,768 bytes of partials for at most 1024 blocks, plus the ticket; every GPU that loads the library holds it until
+ * exit), and never calls cudaMalloc, cudaFree or an allocating library routine. A device whose launch would need more
+ * than 1024 blocks gets CAIRN_B200_ERR_SCRATCH. The first call on each device looks up the array's device address;
+ * make it before any stream capture. All calls share the array: calls whose work overlaps on the GPU race, so order
+ * them (one stream). Same result bits as cairn_b200_sum_f32. */
+int cairn_b200_sum_f32_noalloc(void* stream, size_t n, const float* x, float* out);
 
 /* ---- status ----------------------------------------------------------------------------------------------------
  * Waits for `stream`, then reports a CUDA error or a device-side fault recorded by this library's kernels on the
