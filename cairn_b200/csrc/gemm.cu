@@ -24,6 +24,7 @@
 // k == 0, run the SIMT tile kernel at the end of this file, which computes the same products.
 #include <atomic>
 #include <cstdint>
+#include <cstdlib>
 #include <cstring>
 #include <cuda.h>
 #include <cuda_bf16.h>
@@ -324,6 +325,220 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// The two-SM multiply: a cluster of two CTAs (a pair) computes a 256 x (256 G) tile with tcgen05.mma.cta_group::2,
+// G = 1 or 2 column groups of 256. Each CTA stages its own half of the operands at the same shared-memory offsets:
+// rows [128 r, 128 r + 128) of the tile's A, and in each column group g the columns [256 g + 128 r, + 128) of B,
+// for pair rank r. The leader (rank 0) issues one pair MMA per column group and 32-byte k step; each MMA reads both
+// CTAs' halves and accumulates rows 128 r .. 128 r + 127, 256 columns, into rank r's tensor memory.
+//   Why two shapes: the operands reach the SMs from L2 at about 10 TB/s on a B200, and a 256 x 256 pair step
+//   (64 KB per 128-byte k slice per pair) saturates that near 1.3 PFLOP/s. A 256 x 512 tile (G = 2) reads A once for
+//   both column groups, 25 % fewer bytes per flop, at the price of a single accumulator (512 TMEM columns) whose
+//   drain the next tile waits for; G = 1 keeps two accumulators and hides the drain. Eight epilogue warps (two per
+//   TMEM lane quarter, each draining half the columns) keep that drain short.
+//   Both CTAs' TMA loads count their bytes on the leader's "full" barrier; the leader's commits arrive on the
+//   "empty" and "tmem full" barriers of both CTAs (one plain commit per CTA); every epilogue warp of the pair
+//   arrives on the leader's "tmem empty" barrier.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int PAIR_BN = 256;  // columns per MMA (and per column group); each CTA stages half of each group
+
+template <int G> struct PairShape {
+  static constexpr int B_HALF = G * (PAIR_BN / 2) * SLICE;         // 16 KiB per column group
+  static constexpr int STAGES = (200 * 1024) / (A_STAGE + B_HALF);  // 6 (G = 1) or 4 (G = 2)
+  static constexpr int ACCS = G == 1 ? 2 : 1;                       // accumulators in TMEM
+  static constexpr int TMEM_COLS = 512;
+  static constexpr int EPI_WARPS = 8;                               // two warps per TMEM lane quarter
+  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
+  static constexpr int TILE_N = G * PAIR_BN;
+  static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_HALF) + 256;
+};
+
+template <int FMT, int G>
+__global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
+    tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                        const TcParams p) {
+  using F = Fmt<FMT>;
+  using S = PairShape<G>;
+  constexpr int STAGES = S::STAGES;
+  constexpr int CH = SLICE / F::bytes;
+  constexpr int MMA_K_BYTES = 32;
+  constexpr int MMA_K_ROWS = MMA_K_BYTES / F::bytes;
+  constexpr int HALF = PAIR_BN / 2;               // rows of A, and columns of B per group, each CTA stages
+  constexpr int GROUP_BYTES = HALF * SLICE;       // one column group's half in a stage
+  constexpr int COLS_PER_WARP = S::TILE_N / 2;    // each of the two warps on a lane quarter drains half the columns
+
+  extern __shared__ std::uint8_t smem_raw[];
+  std::uint8_t* base = reinterpret_cast<std::uint8_t*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) &
+                                                       ~static_cast<std::uintptr_t>(1023));
+  std::uint8_t* a_smem = base;
+  std::uint8_t* b_smem = base + STAGES * A_STAGE;
+  std::uint64_t* bars = reinterpret_cast<std::uint64_t*>(b_smem + STAGES * S::B_HALF);
+  std::uint64_t* full = bars;
+  std::uint64_t* empty = bars + STAGES;
+  std::uint64_t* tfull = bars + 2 * STAGES;
+  std::uint64_t* tempty = tfull + 2;
+  std::uint64_t* drain = tempty + 2;
+  std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(drain + 1);
+  volatile std::uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const std::uint32_t rank = cluster_rank();
+  const int pair = blockIdx.x / 2, pairs = gridDim.x / 2;
+  const int num_m = (p.m + 2 * HALF - 1) / (2 * HALF), num_n = (p.n + S::TILE_N - 1) / S::TILE_N;
+  const int tiles = num_m * num_n;
+  const int num_kb = (p.k + CH - 1) / CH;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 2 * S::EPI_WARPS);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0u;
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, S::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // both CTAs' barriers exist before either side's copies or arrivals reach them
+  tc_fence_after();
+  const std::uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_a);
+      tma_prefetch_desc(&tm_b);
+      std::uint32_t stage = 0, phase = 0;
+      for (int t = pair; t < tiles; t += pairs) {
+        int mb, nb;
+        tile_of(t, num_m, num_n, mb, nb);
+        const int m0 = mb * 2 * HALF + static_cast<int>(rank) * HALF;  // this CTA's rows of A
+        const int n_tile = nb * S::TILE_N;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.fault, FAULT_WAIT_EMPTY)) goto producer_done;
+          const std::uint32_t leader_full = cluster_addr(&full[stage], 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2u * (A_STAGE + S::B_HALF));
+          const std::uint32_t a_dst = smem_u32(a_smem + stage * A_STAGE);
+          const std::uint32_t b_dst = smem_u32(b_smem + stage * S::B_HALF);
+          const int k0 = kb * CH;
+          if (!p.a_mn) {
+            tma_load_2d_pair(a_dst, &tm_a, leader_full, k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < HALF / CH; ++c)
+              tma_load_2d_pair(a_dst + c * CH * SLICE, &tm_a, leader_full, m0 + c * CH, k0);
+          }
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            const int n0 = n_tile + g * PAIR_BN + static_cast<int>(rank) * HALF;  // this CTA's columns of group g
+            const std::uint32_t dst = b_dst + g * GROUP_BYTES;
+            if (p.b_k) {
+              tma_load_2d_pair(dst, &tm_b, leader_full, k0, n0);
+            } else {
+#pragma unroll
+              for (int c = 0; c < HALF / CH; ++c)
+                tma_load_2d_pair(dst + c * CH * SLICE, &tm_b, leader_full, n0 + c * CH, k0);
+            }
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    producer_done:;
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      const std::uint32_t idesc =
+          idesc_make(F::code, F::code, p.a_mn != 0, p.b_k == 0, static_cast<std::uint32_t>(2 * HALF), PAIR_BN);
+      constexpr bool MN32 = F::bytes == 4;
+      const std::uint32_t a_layout = (MN32 && p.a_mn) ? LAYOUT_SW128_32B : LAYOUT_SW128;
+      const std::uint32_t b_layout = (MN32 && !p.b_k) ? LAYOUT_SW128_32B : LAYOUT_SW128;
+      const std::uint32_t a_sbo = a_layout == LAYOUT_SW128_32B ? 512u : 1024u;
+      const std::uint32_t b_sbo = b_layout == LAYOUT_SW128_32B ? 512u : 1024u;
+      const std::uint32_t a_lbo = p.a_mn ? CH * SLICE : 16u, b_lbo = p.b_k ? 16u : CH * SLICE;
+      std::uint32_t stage = 0, phase = 0, it = 0;
+      for (int t = pair; t < tiles; t += pairs, ++it) {
+        const std::uint32_t acc = S::ACCS == 2 ? (it & 1u) : 0u;
+        const std::uint32_t acc_phase = S::ACCS == 2 ? ((it >> 1) & 1u) : (it & 1u);
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.fault, FAULT_WAIT_TEMPTY)) goto mma_done;
+        tc_fence_after();
+        const std::uint32_t d_tmem = tmem_base + acc * PAIR_BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, abort_flag, p.fault, FAULT_WAIT_FULL)) goto mma_done;
+          tc_fence_after();
+          const std::uint32_t a_addr = smem_u32(a_smem + stage * A_STAGE);
+          const std::uint32_t b_addr = smem_u32(b_smem + stage * S::B_HALF);
+#pragma unroll
+          for (int kk = 0; kk < SLICE / MMA_K_BYTES; ++kk) {
+            const std::uint32_t a_off = p.a_mn ? kk * (MMA_K_ROWS / 8) * 1024 : kk * MMA_K_BYTES;
+            const std::uint32_t b_off = p.b_k ? kk * MMA_K_BYTES : kk * (MMA_K_ROWS / 8) * 1024;
+            const std::uint64_t a_desc = sdesc(a_addr + a_off, a_lbo, a_sbo, a_layout);
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+              umma_pair<F::kind>(d_tmem + g * PAIR_BN, a_desc,
+                                 sdesc(b_addr + g * GROUP_BYTES + b_off, b_lbo, b_sbo, b_layout), idesc,
+                                 (kb | kk) != 0 ? 1u : 0u);
+          }
+          tc_commit_pair(cluster_addr(&empty[stage], 0));
+          tc_commit_pair(cluster_addr(&empty[stage], 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        tc_commit_pair(cluster_addr(&tfull[acc], 0));
+        tc_commit_pair(cluster_addr(&tfull[acc], 1));
+      }
+    mma_done:
+      tc_commit_pair(cluster_addr(drain, 0));
+      drain_wait(drain, 0u, p.fault);
+    }
+    __syncwarp();
+  } else {
+    const int quarter = warp & 3;                       // TMEM lanes 32 * (warp id % 4) .. + 31
+    const int col0 = ((warp - 2) / 4) * COLS_PER_WARP;  // this warp's half of the tile's columns
+    std::uint32_t it = 0;
+    for (int t = pair; t < tiles; t += pairs, ++it) {
+      const std::uint32_t acc = S::ACCS == 2 ? (it & 1u) : 0u;
+      const std::uint32_t acc_phase = S::ACCS == 2 ? ((it >> 1) & 1u) : (it & 1u);
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.fault, FAULT_WAIT_TFULL)) break;
+      tc_fence_after();
+      int mb, nb;
+      tile_of(t, num_m, num_n, mb, nb);
+      const int row = mb * 2 * HALF + static_cast<int>(rank) * HALF + quarter * 32 + lane;
+      const std::uint32_t t_row = tmem_base + (static_cast<std::uint32_t>(quarter * 32) << 16) + acc * PAIR_BN;
+#pragma unroll 1
+      for (int c = col0; c < col0 + COLS_PER_WARP; c += 32) {
+        std::uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c, r);
+        tmem_wait_ld();
+        if (c + 32 == col0 + COLS_PER_WARP) {  // this warp's part of the accumulator is in registers
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+        }
+        store_chunk<FMT>(p, row, nb * S::TILE_N + c, r);
+      }
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync();  // every pair MMA has landed in both CTAs' TMEM and every remote arrival is done
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // The SIMT tile kernel: shapes the tensor maps cannot describe (a row not on 16 bytes), and k == 0. 64 x 64 tiles,
 // 256 threads of 4 x 4 outputs, k in steps of 16 staged through shared memory as f32 (every storage float widens to
 // f32 exactly; tf32 operands are used at full f32 precision here).
@@ -473,6 +688,19 @@ int esize_of(int fmt) { return fmt == FMT_TF32 ? 4 : (fmt == FMT_E4M3 || fmt == 
 
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
 
+// Which tile runs: 0 the one-SM 128 x BN tile, 1 the pair's 256 x 256, 2 the pair's 256 x 512. The pair tiles pay
+// off once both extents fill them, 256 x 512 wherever n allows it. CAIRN_B200_PAIR=0, 1 or 2 pins the choice for
+// measuring the kernels against each other (whichever runs computes the whole product).
+int pair_path(const GemmArgs& g) {
+  static const int pinned = [] {
+    const char* v = std::getenv("CAIRN_B200_PAIR");
+    return (v && v[0] >= '0' && v[0] <= '2') ? v[0] - '0' : -1;
+  }();
+  if (g.m < 256 || g.n < 256) return 0;
+  if (pinned >= 0) return pinned;
+  return g.n >= 512 ? 2 : 1;
+}
+
 template <int FMT, int BN>
 cudaError_t launch_tc(const GemmArgs& g, const TcParams& p, cudaStream_t stream, int sms) {
   using S = Shape<BN>;
@@ -501,6 +729,47 @@ cudaError_t launch_tc(const GemmArgs& g, const TcParams& p, cudaStream_t stream,
   return cudaGetLastError();
 }
 
+template <int FMT, int G>
+cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t stream, int sms) {
+  using S = PairShape<G>;
+  constexpr int CH = SLICE / Fmt<FMT>::bytes;
+  constexpr int HALF = PAIR_BN / 2;
+  const int es = Fmt<FMT>::bytes;
+  CUtensorMap ta, tb;
+  const bool ok_a = g.trans_a ? encode(&ta, FMT, g.a, g.m, g.k, es, CH, CH, true)
+                              : encode(&ta, FMT, g.a, g.k, g.m, es, CH, HALF, false);
+  const bool ok_b = g.trans_b ? encode(&tb, FMT, g.b, g.k, g.n, es, CH, HALF, false)
+                              : encode(&tb, FMT, g.b, g.n, g.k, es, CH, CH, true);
+  if (!ok_a || !ok_b) return cudaErrorInvalidValue;
+  static std::atomic<std::uint64_t> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const std::uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load(std::memory_order_acquire) & bit)) {
+    e = cudaFuncSetAttribute(tc_gemm_pair_kernel<FMT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
+    if (e != cudaSuccess) return e;
+    configured.fetch_or(bit, std::memory_order_acq_rel);
+  }
+  const int tiles = ((p.m + 2 * HALF - 1) / (2 * HALF)) * ((p.n + S::TILE_N - 1) / S::TILE_N);
+  const int pairs = tiles < sms / 2 ? tiles : sms / 2;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(S::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = S::SMEM;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G>, ta, tb, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
 template <int FMT> cudaError_t launch_simt(const GemmArgs& g, const TcParams& p, cudaStream_t stream, int sms) {
   const int tiles = ((p.m + 63) / 64) * ((p.n + 63) / 64);
   const int grid = tiles < sms * 8 ? tiles : sms * 8;
@@ -510,6 +779,11 @@ template <int FMT> cudaError_t launch_simt(const GemmArgs& g, const TcParams& p,
 
 template <int FMT> cudaError_t dispatch(const GemmArgs& g, const TcParams& p, cudaStream_t s, int sms, bool tc) {
   if (!tc) return launch_simt<FMT>(g, p, s, sms);
+  switch (pair_path(g)) {
+    case 1: return launch_pair<FMT, 1>(g, p, s, sms);
+    case 2: return launch_pair<FMT, 2>(g, p, s, sms);
+    default: break;
+  }
   if (p.n > 128) return launch_tc<FMT, 256>(g, p, s, sms);
   return launch_tc<FMT, 128>(g, p, s, sms);
 }

@@ -87,7 +87,7 @@ __device__ __forceinline__ bool mbar_wait(std::uint64_t* bar, std::uint32_t pari
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// TMA (bulk tensor copies, global -> shared, completion counted on an mbarrier). No multicast anywhere.
+// TMA (bulk tensor copies, global -> shared, completion counted on an mbarrier). Every copy lands in one CTA only.
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<std::uint64_t>(map)) : "memory");
@@ -162,6 +162,77 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(std::uint32_t taddr, std::uin
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------------------------------
+// CTA pairs (a cluster of 2): the two-SM MMA (cta_group::2). Every copy and every arrival targets one CTA.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ std::uint32_t cluster_rank() {
+  std::uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// All threads of both CTAs; orders the release of everything before it against everything after it.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// The shared::cluster address of this CTA's shared-memory object `p` as it lies in CTA `rank` of the cluster.
+__device__ __forceinline__ std::uint32_t cluster_addr(const void* p, std::uint32_t rank) {
+  std::uint32_t out;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
+  return out;
+}
+// One arrival on an mbarrier anywhere in the cluster.
+__device__ __forceinline__ void mbar_arrive_cluster(std::uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+// A TMA load into this CTA's shared memory whose completed bytes count on `cluster_bar`, an mbarrier of either CTA
+// of the pair.
+__device__ __forceinline__ void tma_load_2d_pair(std::uint32_t dst, const CUtensorMap* map, std::uint32_t cluster_bar,
+                                                 std::int32_t x, std::int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(dst),
+      "l"(reinterpret_cast<std::uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(std::uint32_t* slot, std::uint32_t cols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(std::uint32_t taddr, std::uint32_t cols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(cols) : "memory");
+}
+// Arrives once on `cluster_bar` (either CTA of the pair) when every pair MMA this thread issued has completed.
+__device__ __forceinline__ void tc_commit_pair(std::uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+// The pair MMA: D (128 lanes of each CTA's TMEM) (+)= A (each CTA's half of the rows) * B (each CTA's half of the
+// columns), both halves at the same shared-memory offsets the descriptors name.
+template <int KIND>
+__device__ __forceinline__ void umma_pair(std::uint32_t d_tmem, std::uint64_t a_desc, std::uint64_t b_desc,
+                                          std::uint32_t idesc, std::uint32_t accumulate) {
+  if constexpr (KIND == KIND_F16) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  } else if constexpr (KIND == KIND_TF32) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  } else {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+  }
+}
 
 // ---------------------------------------------------------------------------------------------------------------
 // UMMA descriptors (the sm_100 shared-memory matrix descriptor and the kind::f16/tf32/f8f6f4 instruction descriptor)

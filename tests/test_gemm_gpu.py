@@ -220,3 +220,34 @@ def test_tf32_every_operand_layout(cuda, trans_a, trans_b):
     want = a.astype(np.float64) @ b.astype(np.float64)
     tol = (2.0**-9 + (k + 1) * 2.0**-22) * (np.abs(a).astype(np.float64) @ np.abs(b).astype(np.float64))
     assert (np.abs(got - want) <= tol).all()
+
+
+@pytest.mark.parametrize("fmt", inputs.FORMATS)
+@pytest.mark.parametrize("shape", [(256, 256, 64), (384, 520, 200), (257, 264, 72), (1024, 768, 1000)])
+def test_the_two_sm_pair_tile_against_the_oracle(cuda, fmt, shape):
+    """m and n of 256 or more run the cta_group::2 kernel (256 x 256 tiles over CTA pairs)."""
+    m, n, k = shape
+    c, a, b = inputs.mma_case(fmt, m, n, k, seed=sum(shape))
+    want = restated.mma(fmt, c, a, b, m, n, k)
+    got = device_mma(fmt, c, a, b, m, n, k, cuda)
+    ok = within(got, want, 2 * bound(fmt, c, a, b, m, n, k))
+    assert ok.all(), (fmt, shape, np.argwhere(~ok)[:4].ravel())
+
+
+@pytest.mark.parametrize("trans_a,trans_b", [(False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("fmt", ["bf16", "f16", "f8e4m3"])
+def test_the_pair_tile_with_transposed_operands(cuda, fmt, trans_a, trans_b):
+    m, n, k = 320, 392, 264
+    rng = np.random.default_rng(3)
+    a = inputs.encode(fmt, rng.standard_normal(m * k))
+    b = inputs.encode(fmt, rng.standard_normal(k * n))
+    av = inputs.decode(fmt, a).reshape(m, k)
+    bv = inputs.decode(fmt, b).reshape(k, n)
+    a_st = np.ascontiguousarray(a.reshape(m, k).T) if trans_a else a.reshape(m, k)
+    b_st = np.ascontiguousarray(b.reshape(k, n).T) if trans_b else b.reshape(k, n)
+    got = cairn_b200.gemm(to_dev(fmt, a_st, cuda).view(a_st.shape), to_dev(fmt, b_st, cuda).view(b_st.shape),
+                          trans_a=trans_a, trans_b=trans_b).cpu().numpy()
+    cairn_b200.stream_status()
+    want = av @ bv
+    tol = 2 * (k + 1) * 2.0**-22 * (np.abs(av) @ np.abs(bv))
+    assert (np.abs(got - want) <= tol).all()
