@@ -105,7 +105,7 @@ def profile_traffic(name: str) -> int | None:
 
 
 class ClockSampler:
-    """nvidia-smi samples of SM clock and throttle reasons every 100 ms; `window` keeps those inside [t0, t1]."""
+    """nvidia-smi samples of SM clock and throttle reasons every 50 ms; `window` keeps those inside [t0, t1]."""
 
     QUERY = ("clocks.sm,clocks.max.sm,clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
@@ -116,7 +116,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-i", str(index),
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except (FileNotFoundError, OSError):
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
@@ -142,7 +142,7 @@ class ClockSampler:
         if not inside and self.samples:  # a timed region shorter than the sampling period: the nearest samples
             nearest = sorted(self.samples, key=lambda ts: min(abs(ts[0] - t0), abs(ts[0] - t1)))[:3]
             inside = [s for _, s in nearest]
-            note = "timed region shorter than the 100 ms sampling period: nearest samples of the same run"
+            note = "timed region shorter than the 50 ms sampling period: nearest samples of the same run"
         if not inside:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
@@ -362,7 +362,7 @@ class Stream:
         elif workload == "sum_f32":
             self.x = torch.rand(self.n, device=dev, generator=g) * 2 - 1
             self.part = torch.zeros(3, dtype=torch.float64, device=dev)
-            self.parts = torch.zeros(dist.world, 3, dtype=torch.float64, device=dev)
+            self.parts = torch.zeros(dist.world * 3, dtype=torch.float64, device=dev)
             self.total = torch.zeros(1, dtype=torch.float32, device=dev)
             self.bytes = 4
         else:
