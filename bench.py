@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of CAIRN's data-parallel hot path on B200, one JSON line per run (rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm|saxpy|sum_f32|sum_u64|gemm5]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm|gemm5|mlp|saxpy|sum_f32|sum_u64]
                     [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...        (one rank per GPU, NCCL)
 
@@ -11,6 +11,8 @@ Workloads (the default is the one the headline metric is 
            with the same B (the M-sharded row-block partition, no collective): weak scaling.
   gemm5    config 5: M-sharded bf16 GEMM, M = 65536, N = K = 8192, f32 out; rank r computes rows [r M/N, (r+1) M/N):
            strong scaling (total work fixed).
+  mlp      config 3: a 2-layer MLP's forward + backward (batch 8192, 4096 -> 16384 -> 4096): six products and the
+           fused MSE kernel per step; one replica per rank: weak scaling.
   saxpy    config 4: out = 2.5 x + y over n = 2^30 f32, range-sharded: strong scaling.
   sum_f32  config 4: `reduce +` over n = 2^30 f32 (exact sum rounded once), range-sharded; the ranks' parts meet in
            one NCCL all-gather and a combine kernel on every rank.
@@ -428,6 +430,71 @@ class Stream:
         return self.dist.world * chunk * self.bytes / (ms * 1e-3) / 1e9, h2d, d2h
 
 
+class Mlp:
+    """Config 3: one forward + backward of a 2-layer MLP (batch 8192, 4096 -> 16384 -> 4096, bf16 weights ~ N(0, 0.02),
+    inputs ~ N(0, 1), ReLU, MSE against an N(0, 1) target): six products and the fused loss kernel per step.
+    Replicas only at N GPUs (each rank runs its own step): weak scaling."""
+
+    def __init__(self, dist: Dist):
+        import torch
+
+        from cairn_b200 import mlp
+
+        self.torch, self.dist, self.mlp = torch, dist, mlp
+        self.B, self.D, self.H, self.O = 8192, 4096, 16384, 4096
+        dev = dist.device
+        g = torch.Generator(device=dev).manual_seed(0 + dist.rank)
+        self.x = torch.randn(self.B, self.D, device=dev, generator=g).bfloat16()
+        self.w1 = (torch.randn(self.D, self.H, device=dev, generator=g) * 0.02).bfloat16()
+        self.w2 = (torch.randn(self.H, self.O, device=dev, generator=g) * 0.02).bfloat16()
+        self.t = torch.randn(self.B, self.O, device=dev, generator=g)
+        self.ws = mlp.MLPWorkspace(self.B, self.D, self.H, self.O, dev)
+        self.stream = torch.cuda.current_stream(dev)
+        self.flops = mlp.mlp_flops(self.B, self.D, self.H, self.O)
+        self.scaling = "weak"
+
+    def launch(self, i: int):
+        self.mlp.mlp_step(self.x, self.w1, self.w2, self.t, self.ws, self.stream.cuda_stream)
+
+    def e2e(self, steps: int, warmup: int):
+        """The step through the C ABI with this step's batch and target copied in from pinned host memory and the
+        loss read back; the weights stay resident as in training."""
+        torch = self.torch
+        x_h, t_h = self.x.cpu().pin_memory(), self.t.cpu().pin_memory()
+        loss_h = torch.empty(1, dtype=torch.float32).pin_memory()
+
+        def step(i):
+            self.x.copy_(x_h, non_blocking=True)
+            self.t.copy_(t_h, non_blocking=True)
+            self.launch(i)
+            loss_h.copy_(self.ws.loss, non_blocking=True)
+
+        ms, _, _, _ = time_steps(self.dist, self.stream, step, steps, warmup, per_launch=False)
+        return self.dist.world * self.flops / (ms * 1e-3) / 1e12, x_h.numel() * 2 + t_h.numel() * 4, 4
+
+
+def cpu_mlp_sample(budget_s: float):
+    """GFLOP/s of the oracle's restatement of derive grad's dense-layer loops (single-threaded; the reference's own
+    derive-grad output needs its compiler, which is not run here) on a reduced shape, scaled to TFLOP/s."""
+    import numpy as np
+
+    from oracle import restated
+
+    B, D, H, O = 32, 256, 1024, 256
+    rng = np.random.default_rng(0)
+    x = rng.integers(0, 1 << 16, B * D, dtype=np.uint16) & np.uint16(0x3FFF)
+    w1 = rng.integers(0, 1 << 16, D * H, dtype=np.uint16) & np.uint16(0x3CFF)
+    w2 = rng.integers(0, 1 << 16, H * O, dtype=np.uint16) & np.uint16(0x3CFF)
+    t = rng.standard_normal(B * O).astype(np.float32)
+    spent, flops = 0.0, 0.0
+    while spent < budget_s:
+        t0 = time.perf_counter()
+        restated.mlp_step(x, w1, w2, t, B, D, H, O)
+        spent += time.perf_counter() - t0
+        flops += 2.0 * B * H * (3 * D + 3 * O)
+    return flops / spent / 1e12, 1, "port", f"{int(flops / (2.0 * B * H * 6 * D))} steps at batch 32, 256 -> 1024 -> 256"
+
+
 # ---------------------------------------------------------------------------------------------------------------------
 def reference_arm(args, dist: Dist) -> None:
     """The reference's own CPU implementation of the path (the CAIRN runtime's host code, oracle/_ref) on this box's
@@ -437,7 +504,12 @@ def reference_arm(args, dist: Dist) -> None:
     from oracle import reference
 
     budget = max(0.2, min(5.0, 90.0 / max(1, args.steps + args.warmup)))
-    if args.workload in ("gemm", "gemm5"):
+    if args.workload == "mlp":
+        for _ in range(args.warmup):
+            cpu_mlp_sample(budget / 4)
+        vals = [cpu_mlp_sample(budget) for _ in range(args.steps)]
+        unit, sample = "TFLOP/s", vals[-1][3]
+    elif args.workload in ("gemm", "gemm5"):
         m, n, k = (4096, 4096, 4096) if args.workload == "gemm" else (65536, 8192, 8192)
         for _ in range(args.warmup):
             cpu_gemm_sample(m, n, k, budget / 4)
@@ -452,8 +524,9 @@ def reference_arm(args, dist: Dist) -> None:
     cores, kind = vals[-1][1], vals[-1][2]
     line = {"metric": BASELINE_METRIC, "value": value, "unit": unit, "impl": "reference", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True,
-            "scaling": "weak" if args.workload == "gemm" else "strong", "vs_baseline": None,
-            "dtype": "bf16" if args.workload.startswith("gemm") else ("f32" if args.workload != "sum_u64" else "u64"),
+            "scaling": "weak" if args.workload in ("gemm", "mlp") else "strong", "vs_baseline": None,
+            "dtype": "bf16" if args.workload in ("gemm", "gemm5", "mlp") else
+                     ("f32" if args.workload != "sum_u64" else "u64"),
             "data": "synthetic", "config": config_of(args, dist),
             "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind,
                              "sample": f"per step: {sample}"},
@@ -469,6 +542,10 @@ def config_of(args, dist: Dist) -> dict:
         return {"workload": "config 2: bf16 GEMM 4096^3, fused bias + ReLU, bf16 out", "m": 4096 * dist.world,
                 "n": 4096, "k": 4096, "rows_per_gpu": 4096, "parallelism": f"row-block x{dist.world}",
                 "l2": "inputs rotate over buffer sets larger than L2"}
+    if w == "mlp":
+        return {"workload": "config 3: 2-layer MLP forward + backward (6 products + fused MSE)", "batch": 8192,
+                "dims": [4096, 16384, 4096], "parallelism": f"replicas x{dist.world}",
+                "l2": "operands far larger than L2"}
     if w == "gemm5":
         return {"workload": "config 5: M-sharded bf16 GEMM, f32 out", "m": 65536, "n": 8192, "k": 8192,
                 "parallelism": f"row-block x{dist.world}", "l2": "inputs rotate over buffer sets larger than L2"}
@@ -481,12 +558,13 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
-    ap.add_argument("--workload", default="gemm", choices=["gemm", "gemm5", "saxpy", "sum_f32", "sum_u64"])
+    ap.add_argument("--workload", default="gemm", choices=["gemm", "gemm5", "mlp", "saxpy", "sum_f32", "sum_u64"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--log2n", type=int, default=30, help="saxpy/sum size 2^log2n (BASELINE: 30; smaller for ncu)")
     args = ap.parse_args()
-    defaults = {"gemm": (2000, 50), "gemm5": (50, 5), "saxpy": (100, 5), "sum_f32": (200, 5), "sum_u64": (100, 5)}
+    defaults = {"gemm": (2000, 50), "gemm5": (50, 5), "mlp": (40, 5), "saxpy": (100, 5), "sum_f32": (200, 5),
+                "sum_u64": (100, 5)}
     d_steps, d_warm = defaults[args.workload] if args.impl == "ours" else (5, 1)
     args.steps = args.steps if args.steps is not None else d_steps
     args.warmup = args.warmup if args.warmup is not None else d_warm
@@ -500,8 +578,12 @@ def main() -> None:
         return
     import torch
 
-    wl = Gemm(dist, args.workload == "gemm5") if args.workload.startswith("gemm") else \
-        Stream(dist, args.workload, args.log2n)
+    if args.workload.startswith("gemm"):
+        wl = Gemm(dist, args.workload == "gemm5")
+    elif args.workload == "mlp":
+        wl = Mlp(dist)
+    else:
+        wl = Stream(dist, args.workload, args.log2n)
     peaks, peak_source = measured_peaks()
     sampler = ClockSampler(dist.local)
     ms, launch_ms, t0, t1 = time_steps(dist, wl.stream, wl.launch, args.steps, args.warmup)
@@ -512,13 +594,16 @@ def main() -> None:
         raise SystemExit(f"device status {stat} after the timed steps")
     e2e_val, h2d, d2h = wl.e2e(max(3, min(args.steps, 20)), 3)
 
-    if isinstance(wl, Gemm):
+    if isinstance(wl, (Gemm, Mlp)):
         value = dist.world * wl.flops / (ms * 1e-3) / 1e12
         unit, bound, dtype = "TFLOP/s", "tensor", "bf16"
+        # an MLP step is six equal products and a short loss kernel: the products are credited with the whole step
         achieved = wl.flops / (launch_ms * 1e-3) / 1e12
-        peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
-        kernel = "tc_gemm_kernel"
-        traffic = profile_traffic("gemm_bf16_4096_bias_relu" if args.workload == "gemm" else "gemm_bf16_config5")
+        long_step = isinstance(wl, Mlp) or args.workload == "gemm5"
+        peak = peaks.get("bf16_tflops_sustained" if long_step else "bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+        kernel = "tc_gemm_pair_kernel"
+        traffic = profile_traffic({"gemm": "gemm_bf16_4096_bias_relu", "gemm5": "gemm_bf16_config5",
+                                   "mlp": "mlp_step_config3"}[args.workload])
     else:
         per_rank_bytes = wl.n * wl.bytes
         value = dist.world * per_rank_bytes / (ms * 1e-3) / 1e9
@@ -531,21 +616,25 @@ def main() -> None:
 
     cpu = None
     if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
-        if isinstance(wl, Gemm):
+        if isinstance(wl, Mlp):
+            v, cores, kind, sample = cpu_mlp_sample(12.0)
+        elif isinstance(wl, Gemm):
             v, cores, kind, sample = cpu_gemm_sample(wl.m, wl.n, wl.k, 12.0)
         else:
             v, cores, kind, sample = cpu_stream_sample(args.workload, 12.0)
         cpu = {"value": v, "unit": unit, "cores": cores, "kind": kind, "sample": sample}
 
-    launches = args.steps * (1 if isinstance(wl, Gemm) or args.workload != "sum_f32" or dist.world == 1 else 2)
+    launches = args.steps * (7 if isinstance(wl, Mlp) else
+                             1 if isinstance(wl, Gemm) or args.workload != "sum_f32" or dist.world == 1 else 2)
     line = {
         "metric": BASELINE_METRIC, "value": value, "unit": unit, "n_gpus": dist.world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": wl.scaling
-        if isinstance(wl, Gemm) else "strong", "vs_baseline": None, "dtype": dtype,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+        "scaling": wl.scaling if isinstance(wl, (Gemm, Mlp)) else "strong", "vs_baseline": None, "dtype": dtype,
         "data": "synthetic (seeded device generators; random-init operands of the configs' shapes and distributions)",
         "config": config_of(args, dist),
         "roofline": {"bound": bound, "kernel": kernel, "achieved": achieved, "peak": peak, "unit": unit,
-                     "frac": achieved / peak, "peak_source": f"{peak_source} ({'bf16_tflops burst' if bound == 'tensor' else 'hbm_gbs'})",
+                     "frac": achieved / peak,
+                     "peak_source": f"{peak_source} ({'hbm_gbs' if bound == 'hbm' else ('bf16_tflops_sustained: a long step' if isinstance(wl, Mlp) or args.workload == 'gemm5' else 'bf16_tflops burst')})",
                      "traffic": traffic},
         "cpu_baseline": cpu,
         "clocks": clocks,

@@ -36,6 +36,8 @@ SIGNATURES: dict[str, tuple] = {
     "cairn_b200_mma_f8e5m2": (_i, [_p, _z, _z, _z, _p, _z, _p, _z, _p, _z]),
     "cairn_b200_mma_tf32": (_i, [_p, _z, _z, _z, _p, _z, _p, _z, _p, _z]),
     "cairn_b200_gemm": (_i, [_p, _i, _z, _z, _z, _p, _i, _p, _i, _p, _i, _p, _i]),
+    "cairn_b200_gemm_relu_grad": (_i, [_p, _i, _z, _z, _z, _p, _i, _p, _i, _p, _p]),
+    "cairn_b200_mse_grad": (_i, [_p, _z, _p, _p, _p, _p]),
     "cairn_b200_saxpy_f32": (_i, [_p, _z, _p, _p, _p, _f]),
     "cairn_b200_sum_f32": (_i, [_p, _z, _p, _p]),
     "cairn_b200_sum_f32_partial": (_i, [_p, _z, _p, _p]),

@@ -139,7 +139,8 @@ std::size_t format_bytes(int fmt) {
 }
 
 int gemm_entry(cudaStream_t stream, int fmt, std::size_t m, std::size_t n, std::size_t k, const void* a, int trans_a,
-               const void* b, int trans_b, void* out, int out_kind, const float* bias, int act) {
+               const void* b, int trans_b, void* out, int out_kind, const float* bias, int act,
+               const std::uint16_t* mask = nullptr) {
   const std::size_t es = format_bytes(fmt);
   if (!es || (out_kind != OUT_ACC_F32 && out_kind != OUT_STORE_F32 && out_kind != OUT_BF16) ||
       (act != ACT_NONE && act != ACT_RELU) || (trans_a != 0 && trans_a != 1) || (trans_b != 0 && trans_b != 1))
@@ -150,15 +151,16 @@ int gemm_entry(cudaStream_t stream, int fmt, std::size_t m, std::size_t n, std::
   if (!view_ok(a, mk, es, es) || !view_ok(b, kn, es, es) || !view_ok(out, mn, oes, oes)) return CAIRN_B200_ERR_VIEW;
   const bool biased = out_kind == OUT_BF16 && bias != nullptr;
   if (biased && !view_ok(bias, n, 4, 4)) return CAIRN_B200_ERR_VIEW;
+  if (mask && (out_kind != OUT_BF16 || !view_ok(mask, mn, 2, 2))) return CAIRN_B200_ERR_VIEW;
   if (overlaps(out, mn * oes, a, mk * es) || overlaps(out, mn * oes, b, kn * es) ||
-      (biased && overlaps(out, mn * oes, bias, n * 4)))
+      (biased && overlaps(out, mn * oes, bias, n * 4)) || (mask && overlaps(out, mn * oes, mask, mn * 2)))
     return CAIRN_B200_ERR_OVERLAP;
   if (!m || !n) return CAIRN_B200_OK;
   if (!k && out_kind == OUT_ACC_F32) return CAIRN_B200_OK;  // no products: every output keeps its old value
   int status;
   const Device* d = current(&status);
   if (!d) return status;
-  GemmArgs g{fmt, m, n, k, a, trans_a, b, trans_b, out, out_kind, biased ? bias : nullptr, act};
+  GemmArgs g{fmt, m, n, k, a, trans_a, b, trans_b, out, out_kind, biased ? bias : nullptr, act, mask};
   return cuda_status(gemm_launch(g, stream, d->sms, d->fault));
 }
 
@@ -278,6 +280,31 @@ int cairn_b200_gemm(void* stream, int format, size_t m, size_t n, size_t k, cons
                     const void* b, int trans_b, void* out, int out_kind, const float* bias, int act) {
   return gemm_entry(static_cast<cudaStream_t>(stream), format, m, n, k, a, trans_a, b, trans_b, out, out_kind, bias,
                     act);
+}
+
+int cairn_b200_gemm_relu_grad(void* stream, int format, size_t m, size_t n, size_t k, const void* a, int trans_a,
+                              const void* b, int trans_b, uint16_t* out, const uint16_t* mask) {
+  if (!mask) return CAIRN_B200_ERR_VIEW;
+  return gemm_entry(static_cast<cudaStream_t>(stream), format, m, n, k, a, trans_a, b, trans_b, out, OUT_BF16, nullptr,
+                    ACT_NONE, mask);
+}
+
+int cairn_b200_mse_grad(void* stream, size_t n, const float* y, const float* t, uint16_t* dy, float* loss) {
+  if (!view_ok(y, n, 4, 4) || !view_ok(t, n, 4, 4) || !view_ok(dy, n, 2, 2) || !view_ok(loss, 1, 4, 4))
+    return CAIRN_B200_ERR_VIEW;
+  if (overlaps(dy, n * 2, y, n * 4) || overlaps(dy, n * 2, t, n * 4) || overlaps(loss, 4, dy, n * 2) ||
+      overlaps(loss, 4, y, n * 4) || overlaps(loss, 4, t, n * 4))
+    return CAIRN_B200_ERR_OVERLAP;
+  int status;
+  const Device* d = current(&status);
+  if (!d) return status;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  void* scratch = nullptr;
+  if ((status = acquire(*d, s, &scratch)) != CAIRN_B200_OK) return status;
+  const float scale = n ? 2.0f / static_cast<float>(n) : 0.0f;
+  const cudaError_t e = mse_grad_launch(n, y, t, dy, scale, loss, scratch, s, d->sms);
+  const int r = release(s);
+  return e != cudaSuccess ? CAIRN_B200_ERR_CUDA : r;
 }
 
 int cairn_b200_saxpy_f32(void* stream, size_t n, float* out, const float* x, const float* y, float a) {

@@ -52,6 +52,7 @@ struct TcParams {
   void* out;
   const float* bias;
   int act;
+  const std::uint16_t* mask;  // OUT_BF16 only: keep an output where this m x n bf16 array is > 0, else 0
   int vec;        // every output row starts on 16 bytes and holds whole 16-byte groups
   std::uint32_t* fault;
 };
@@ -101,6 +102,12 @@ __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col,
       float x = __fadd_rn(__uint_as_float(r[j]), b);
       if (p.act == ACT_RELU) x = x < 0.0f ? 0.0f : x;
       v[j] = x;
+    }
+    if (p.mask != nullptr) {  // the ReLU's backward: the gradient passes where the forward's output was positive
+      const std::uint16_t* mrow = p.mask + static_cast<std::size_t>(row) * p.n + col;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col + j < p.n && !(__uint_as_float(static_cast<std::uint32_t>(__ldg(mrow + j)) << 16) > 0.0f)) v[j] = 0.0f;
     }
     __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + static_cast<std::size_t>(row) * p.n + col;
     if (p.vec && col + 32 <= p.n) {
@@ -626,6 +633,7 @@ __global__ void __launch_bounds__(256) simt_gemm_kernel(const void* a, const voi
         if (p.out_kind == OUT_BF16) {
           float v = __fadd_rn(acc[i][j], p.bias ? p.bias[col] : 0.0f);
           if (p.act == ACT_RELU) v = v < 0.0f ? 0.0f : v;
+          if (p.mask != nullptr && !(__uint_as_float(static_cast<std::uint32_t>(p.mask[o]) << 16) > 0.0f)) v = 0.0f;
           static_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16_rn(v);
         } else if (p.out_kind == OUT_ACC_F32) {
           float* c = static_cast<float*>(p.out);
@@ -813,6 +821,7 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream, int sms, std::ui
   p.out = g.out;
   p.bias = g.bias;
   p.act = g.act;
+  p.mask = g.mask;
   p.fault = fault;
   const std::uint64_t out_es = g.out_kind == OUT_BF16 ? 2 : 4;
   p.vec = aligned16(g.out) && (g.n * out_es) % 16 == 0;

@@ -13,6 +13,7 @@
 //   - f32 terms are added in f64, which holds every f32 term exactly; the total is rounded to f32 once.
 //   - u64 terms carry cr::Sum's sticky overflow flag (runtime/cairn_runtime.hpp:158-166) through every fold.
 #include <cstdint>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include "gemm.h"
 
@@ -266,6 +267,53 @@ __global__ void combine_f32_parts_kernel(const double* parts, int count, float* 
   *out = r;
 }
 
+// ---- the MLP's loss head: mean-squared error and its gradient in one pass ------------------------------------------
+__device__ __forceinline__ double block_sum_f64(double v, double* shared) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+#pragma unroll
+  for (int off = 16; off; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+  if (lane == 0) shared[warp] = v;
+  __syncthreads();
+  double t = 0.0;
+  if (warp == 0) {
+    t = lane < WARPS ? shared[lane] : 0.0;
+#pragma unroll
+    for (int off = 16; off; off >>= 1) t += __shfl_xor_sync(0xffffffffu, t, off);
+  }
+  __syncthreads();
+  return t;
+}
+
+__global__ void __launch_bounds__(T, 2) mse_grad_kernel(std::size_t n, const float* y, const float* t,
+                                                       __nv_bfloat16* dy, float scale, float* loss,
+                                                       Partial* partials, unsigned int* ticket) {
+  __shared__ double shared[WARPS];
+  __shared__ bool last;
+  const std::size_t stride = static_cast<std::size_t>(gridDim.x) * T;
+  double acc = 0.0;
+  for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x; i < n; i += stride) {
+    const float d = __fsub_rn(__ldcs(y + i), __ldcs(t + i));
+    dy[i] = __float2bfloat16_rn(__fmul_rn(d, scale));
+    acc += static_cast<double>(d) * static_cast<double>(d);  // exact: a product of two f32 fits a double
+  }
+  const double s = block_sum_f64(acc, shared);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x].s = s;
+    __threadfence();
+    last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  double total = 0.0;
+  for (unsigned int b = threadIdx.x; b < gridDim.x; b += T) total += __ldcg(&partials[b].s);
+  total = block_sum_f64(total, shared);
+  if (threadIdx.x == 0) {
+    *loss = __double2float_rn(total / static_cast<double>(n));
+    *ticket = 0u;
+  }
+}
+
 // ---- u64 checked sum --------------------------------------------------------------------------------------------
 struct SumU64 {
   unsigned long long v;
@@ -390,6 +438,16 @@ cudaError_t sum_f32_launch(std::size_t n, const float* x, float* out_f32, double
 
 cudaError_t combine_f32_parts_launch(const double* parts, int count, float* out, cudaStream_t s) {
   combine_f32_parts_kernel<<<1, 32, 0, s>>>(parts, count, out);
+  return cudaGetLastError();
+}
+
+cudaError_t mse_grad_launch(std::size_t n, const float* y, const float* t, std::uint16_t* dy, float scale,
+                            float* loss, void* scratch, cudaStream_t s, int sms) {
+  if (!n) return cudaMemsetAsync(loss, 0, sizeof(float), s);
+  const int grid = stream_grid(sms);
+  Partial* partials = static_cast<Partial*>(scratch);
+  unsigned int* ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(scratch) + static_cast<std::size_t>(grid) * 32);
+  mse_grad_kernel<<<grid, T, 0, s>>>(n, y, t, reinterpret_cast<__nv_bfloat16*>(dy), scale, loss, partials, ticket);
   return cudaGetLastError();
 }
 

@@ -83,6 +83,16 @@ int cairn_b200_mma_tf32(void* stream, size_t m, size_t n, size_t k, float* c, si
 int cairn_b200_gemm(void* stream, int format, size_t m, size_t n, size_t k, const void* a, int trans_a,
                     const void* b, int trans_b, void* out, int out_kind, const float* bias, int act);
 
+/* The backward of a ReLU layer fused into its gradient product: out (bf16, m x n) = op(A) * op(B) rounded to bf16
+ * where mask[i][j] (bf16, m x n: the layer's forward output) is > 0, and 0 elsewhere; derive grad's chain rule
+ * through `relu` (compiler/derive/gradients.py) applied in the product's epilogue. */
+int cairn_b200_gemm_relu_grad(void* stream, int format, size_t m, size_t n, size_t k, const void* a, int trans_a,
+                              const void* b, int trans_b, uint16_t* out, const uint16_t* mask);
+
+/* Mean-squared-error loss and its gradient over n f32 pairs (the MLP step's head): dy[i] = bf16((y[i] - t[i]) *
+ * (2 / n)) and *loss = f32(sum (y[i] - t[i])^2 / n), the sum in f64; loss is a device f32. */
+int cairn_b200_mse_grad(void* stream, size_t n, const float* y, const float* t, uint16_t* dy, float* loss);
+
 /* ---- parallel regions -----------------------------------------------------------------------------------------
  * cr::gpu::run(ctx, n, [=](size_t i) { out[i] = a * x[i] + y[i]; }), runtime/cairn_exec.hpp:103-108 with the lane
  * kernel of runtime/cairn_kernels.hpp:69-96: every i below n once, a * x[i] and the sum each rounded to f32 (the

@@ -111,6 +111,20 @@ class restated:
         return out
 
     @staticmethod
+    def mlp_step(x: np.ndarray, w1: np.ndarray, w2: np.ndarray, t: np.ndarray, B: int, D: int, Hd: int, O: int):
+        """BASELINE config 3's step at any shape: bf16 patterns x (B x D), w1 (D x Hd), w2 (Hd x O), f32 target t.
+        Returns a dict of H, Y, dY, loss, dW2, dH, dW1, dX."""
+        x, w1, w2 = (np.ascontiguousarray(v, np.uint16) for v in (x, w1, w2))
+        t = np.ascontiguousarray(t, np.float32)
+        out = {"H": np.empty(B * Hd, np.uint16), "Y": np.empty(B * O, np.float32), "dY": np.empty(B * O, np.uint16),
+               "loss": np.zeros(1, np.float32), "dW2": np.empty(Hd * O, np.float32),
+               "dH": np.empty(B * Hd, np.uint16), "dW1": np.empty(D * Hd, np.float32), "dX": np.empty(B * D, np.float32)}
+        _rest.fn("mlp_step", None, [_z] * 4 + [_p] * 12)(
+            B, D, Hd, O, _ptr(x), _ptr(w1), _ptr(w2), _ptr(t), *(_ptr(out[k]) for k in
+                                                                 ("H", "Y", "dY", "loss", "dW2", "dH", "dW1", "dX")))
+        return out
+
+    @staticmethod
     def sum_f32(x: np.ndarray) -> np.float32:
         x = np.ascontiguousarray(x, np.float32)
         return np.float32(_rest.fn("sum_f32", _f, [_z, _p])(x.size, _ptr(x)))

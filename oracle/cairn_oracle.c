@@ -18,9 +18,10 @@
  *                         cairn_parallel.hpp:372-378): two roundings, no fused multiply-add.
  *   - oracle_bias_act     the fused epilogue this project adds beside the multiply (the reference has none,
  *                         cairn_tensor.hpp:189-193 only stores the f32 accumulator): bf16(act(f32(acc + bias[j]))).
- *   - oracle_gemm_f32_*   the transposed products the derive-grad backward of a dense layer forms
+ *   - oracle_gemm_t16     the transposed products the derive-grad backward of a dense layer forms
  *                         (compiler/derive/gradients.py:1-11): dX += dY * W^T and dW += X^T * dY, each output a
  *                         sequential f32 sum in increasing p after its old value.
+ *   - oracle_mlp_step     BASELINE config 3's 2-layer MLP forward + MSE + backward from those loops.
  */
 #include <math.h>
 #include <stdint.h>
@@ -263,4 +264,90 @@ void oracle_saxpy_f32(size_t n, float* out, const float* x, const float* y, floa
     volatile float s = p + y[i];
     out[i] = s;
   }
+}
+
+/* ---------------------------------------------------------------------------------------------------------------
+ * The 2-layer MLP step of BASELINE config 3 (forward, MSE loss, backward), with the bf16 storage of the device path
+ * (H, dY, dH in bf16; Y and the weight and input gradients in f32). The backward of each dense layer is the loop
+ * derive grad writes for `out[i][j] = sum_p x[i][p] * w[p][j]` (compiler/derive/gradients.py:1-11; the expanded
+ * form re-runs the forward, then for each output e = (i, j) in order adds d_out[e] * w[p][j] into d_x[i][p] and
+ * x[i][p] * d_out[e] into d_w[p][j] for p in order): d_x = d_out * w^T and d_w = x^T * d_out, every sum sequential in
+ * f32. ReLU's backward passes d where the forward's output is positive. Loss = sum (y - t)^2 / n in f64, rounded;
+ * dY = bf16((y - t) * (2 / n)).
+ * ------------------------------------------------------------------------------------------------------------- */
+void oracle_mlp_step(size_t B, size_t D, size_t Hd, size_t O, const uint16_t* X, const uint16_t* W1,
+                     const uint16_t* W2, const float* T, uint16_t* H, float* Y, uint16_t* dY, float* loss,
+                     float* dW2, uint16_t* dH, float* dW1, float* dX) {
+  for (size_t b = 0; b < B; ++b)
+    for (size_t h = 0; h < Hd; ++h) {
+      float s = 0.0f;
+      for (size_t d = 0; d < D; ++d) {
+        volatile float prod = oracle_bf16_to_f32(X[b * D + d]) * oracle_bf16_to_f32(W1[d * Hd + h]);
+        volatile float sum = s + prod;
+        s = sum;
+      }
+      H[b * Hd + h] = oracle_f32_to_bf16(s < 0.0f ? 0.0f : s);
+    }
+  for (size_t b = 0; b < B; ++b)
+    for (size_t o = 0; o < O; ++o) {
+      float s = 0.0f;
+      for (size_t h = 0; h < Hd; ++h) {
+        volatile float prod = oracle_bf16_to_f32(H[b * Hd + h]) * oracle_bf16_to_f32(W2[h * O + o]);
+        volatile float sum = s + prod;
+        s = sum;
+      }
+      Y[b * O + o] = s;
+    }
+  const size_t n = B * O;
+  const float scale = 2.0f / (float)n;
+  double acc = 0.0;
+  for (size_t i = 0; i < n; ++i) {
+    volatile float d = Y[i] - T[i];
+    volatile float g = d * scale;
+    dY[i] = oracle_f32_to_bf16(g);
+    acc += (double)d * (double)d;
+  }
+  *loss = (float)(acc / (double)n);
+  /* layer 2's backward: dH_acc = dY * W2^T, dW2 = H^T * dY (sequential sums in increasing index) */
+  for (size_t h = 0; h < Hd; ++h)
+    for (size_t o = 0; o < O; ++o) {
+      float s = 0.0f;
+      for (size_t b = 0; b < B; ++b) {
+        volatile float prod = oracle_bf16_to_f32(H[b * Hd + h]) * oracle_bf16_to_f32(dY[b * O + o]);
+        volatile float sum = s + prod;
+        s = sum;
+      }
+      dW2[h * O + o] = s;
+    }
+  for (size_t b = 0; b < B; ++b)
+    for (size_t h = 0; h < Hd; ++h) {
+      float s = 0.0f;
+      for (size_t o = 0; o < O; ++o) {
+        volatile float prod = oracle_bf16_to_f32(dY[b * O + o]) * oracle_bf16_to_f32(W2[h * O + o]);
+        volatile float sum = s + prod;
+        s = sum;
+      }
+      dH[b * Hd + h] = oracle_bf16_to_f32(H[b * Hd + h]) > 0.0f ? oracle_f32_to_bf16(s) : 0;
+    }
+  /* layer 1's backward: dX = dH * W1^T, dW1 = X^T * dH */
+  for (size_t d = 0; d < D; ++d)
+    for (size_t h = 0; h < Hd; ++h) {
+      float s = 0.0f;
+      for (size_t b = 0; b < B; ++b) {
+        volatile float prod = oracle_bf16_to_f32(X[b * D + d]) * oracle_bf16_to_f32(dH[b * Hd + h]);
+        volatile float sum = s + prod;
+        s = sum;
+      }
+      dW1[d * Hd + h] = s;
+    }
+  for (size_t b = 0; b < B; ++b)
+    for (size_t d = 0; d < D; ++d) {
+      float s = 0.0f;
+      for (size_t h = 0; h < Hd; ++h) {
+        volatile float prod = oracle_bf16_to_f32(dH[b * Hd + h]) * oracle_bf16_to_f32(W1[d * Hd + h]);
+        volatile float sum = s + prod;
+        s = sum;
+      }
+      dX[b * D + d] = s;
+    }
 }

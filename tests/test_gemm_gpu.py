@@ -251,3 +251,21 @@ def test_the_pair_tile_with_transposed_operands(cuda, fmt, trans_a, trans_b):
     want = av @ bv
     tol = 2 * (k + 1) * 2.0**-22 * (np.abs(av) @ np.abs(bv))
     assert (np.abs(got - want) <= tol).all()
+
+
+def test_baseline_config_1_f32_gemm_512_cubed(cuda):
+    """BASELINE config 1's f32 GEMM (512^3, A, B ~ U[-1, 1] from seed 0), which the reference runs as a `parallel`
+    region on its host pool: the device form reads the f32 operands as tf32, within the tf32 bound of the oracle's
+    in-order f32 sums."""
+    m = n = k = 512
+    rng = np.random.default_rng(0)
+    a = rng.uniform(-1, 1, m * k).astype(np.float32)
+    b = rng.uniform(-1, 1, k * n).astype(np.float32)
+    c = np.zeros(m * n, np.float32)
+    want = restated.mma("f32", c, a, b, m, n, k)
+    ct = torch.from_numpy(c.copy()).to(cuda)
+    cairn_b200.mma_unordered(m, n, k, ct, torch.from_numpy(a).to(cuda), torch.from_numpy(b).to(cuda))
+    cairn_b200.stream_status()
+    mag = np.abs(a.reshape(m, k)).astype(np.float64) @ np.abs(b.reshape(k, n)).astype(np.float64)
+    tol = (2.0**-9 + (k + 1) * 2.0**-22) * mag
+    assert (np.abs(ct.cpu().numpy().reshape(m, n) - want.reshape(m, n)) <= tol).all()

@@ -1,0 +1,69 @@
+"""BASELINE config 3, the 2-layer MLP forward + backward, on the B200 against the oracle's restatement of derive
+grad's dense-layer loops (oracle_mlp_step), at reduced shapes the oracle finishes in seconds, and against torch's
+own f32 autograd as a second reference. The bf16 intermediates (H, dY, dH) are stored as the oracle stores them;
+results agree within the north star's bf16 tolerance (Frobenius 2e-2), and in practice to about 1e-3."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import cairn_b200
+import inputs
+from cairn_b200 import mlp
+from oracle import restated
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b) -> float:
+    a = np.asarray(a, np.float64).ravel()
+    b = np.asarray(b, np.float64).ravel()
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def _bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16).ravel()
+
+
+@pytest.mark.parametrize("B,D,H,O", [(128, 256, 512, 128), (264, 136, 392, 200), (512, 512, 1024, 512)])
+def test_mlp_step_against_the_oracle(cuda, B, D, H, O):
+    rng = np.random.default_rng(B + D)
+    x = inputs.encode("bf16", rng.standard_normal(B * D))
+    w1 = inputs.encode("bf16", rng.standard_normal(D * H) * 0.02 * 16)
+    w2 = inputs.encode("bf16", rng.standard_normal(H * O) * 0.02 * 16)
+    t = rng.standard_normal(B * O).astype(np.float32)
+    want = restated.mlp_step(x, w1, w2, t, B, D, H, O)
+    dev = lambda bits, shape: torch.from_numpy(bits.view(np.int16).copy()).to(cuda).view(torch.bfloat16).view(shape)
+    ws = mlp.mlp_step(dev(x, (B, D)), dev(w1, (D, H)), dev(w2, (H, O)), torch.from_numpy(t).to(cuda).view(B, O))
+    cairn_b200.stream_status()
+    got_h = inputs.decode("bf16", _bits(ws.h))
+    assert _rel(got_h, inputs.decode("bf16", want["H"])) < 1e-2
+    assert _rel(ws.y.cpu().numpy(), want["Y"]) < 1e-2
+    assert abs(float(ws.loss.item()) - float(want["loss"][0])) <= 1e-3 * abs(float(want["loss"][0]))
+    for name in ("dW2", "dW1", "dX"):
+        assert _rel(getattr(ws, name.lower()).cpu().numpy(), want[name]) < 2e-2, name
+    assert _rel(inputs.decode("bf16", _bits(ws.dh)), inputs.decode("bf16", want["dH"])) < 2e-2
+    # the ReLU mask is exactly where H > 0
+    assert (inputs.decode("bf16", _bits(ws.dh))[got_h <= 0] == 0).all()
+
+
+def test_autograd_backward_runs_the_library_and_matches_torch(cuda):
+    B, D, H, O = 256, 256, 512, 256
+    g = torch.Generator(device=cuda).manual_seed(0)
+    x = torch.randn(B, D, device=cuda, generator=g).bfloat16()
+    w1 = (torch.randn(D, H, device=cuda, generator=g) * 0.05).bfloat16().requires_grad_()
+    w2 = (torch.randn(H, O, device=cuda, generator=g) * 0.05).bfloat16().requires_grad_()
+    xr = x.clone().requires_grad_()
+    t = torch.randn(B, O, device=cuda, generator=g)
+    loss = mlp.MLPLoss.apply(xr, w1, w2, t)
+    loss.backward()
+    cairn_b200.stream_status()
+    # torch's own f32 autograd on the same bf16 values
+    X, W1, W2 = (v.detach().float().requires_grad_() for v in (x, w1, w2))
+    ref = ((torch.relu(X @ W1) @ W2 - t) ** 2).mean()
+    ref.backward()
+    assert abs(loss.item() - ref.item()) <= 1e-2 * ref.item()
+    for got, want in ((xr.grad, X.grad), (w1.grad, W1.grad), (w2.grad, W2.grad)):
+        assert _rel(got.float().cpu().numpy(), want.cpu().numpy()) < 2e-2
