@@ -1,0 +1,107 @@
+// A CAIRN device library in the form cairnc emits it (compiler/lower/codegen.py:438-446 for the checked cf_ entries,
+// compiler/lower/header.py:230-247 for the enqueued cq_ entries, compiler/lower/region_lowering.py:122-183 and
+// compiler/device/tensor.py:69-82 for the bodies): every function's body calls only the runtime's templates,
+// cr::gpu::run, cr::gpu::run_vector, cr::gpu::reduce_on and cr::tensor::launch. It is built against the CAIRN
+// runtime headers with include/cairn_b200/runtime ahead of them on the include path (tests/dropin/build_emitted.py),
+// so the same source runs on the B200 machine and libcairn_b200.so. Test input of tests/test_dropin_gpu.py.
+#include <cstddef>
+#include <cstdint>
+#include "cairn_runtime.hpp"
+#include "cairn_float.hpp"
+#include "cairn_gpu.hpp"
+#include "cairn_cub.hpp"
+#include "cairn_tensor.hpp"
+
+namespace {
+using Sum64 = cr::Sum<std::uint64_t>;
+
+// pub fn saxpy(n, out: rw<f32>[n]@device, x: ro<f32>[n]@device, y: ro<f32>[n]@device, a: f32)
+//   { parallel i in n { out[i] = a * x[i] + y[i]; } }
+void ci_saxpy(std::size_t n, float* out, const float* x, const float* y, float a) {
+  cr::gpu::run(cr::gpu::here(), n, [=] CR_DEVICE(std::size_t i) { out[i] = (a * x[i]) + y[i]; });
+}
+// the same region with `plan saxpy4 { vector 4; }`
+void ci_saxpy4(std::size_t n, float* out, const float* x, const float* y, float a) {
+  cr::gpu::run_vector<4>(
+      cr::gpu::here(), n, cr::gpu::aligned<4>(out, x, y),
+      [=] CR_DEVICE(std::size_t i) { out[i] = (a * x[i]) + y[i]; },
+      [=] CR_DEVICE(std::size_t i) {
+        const auto xv = cr::gpu::Chunk<float, 4>::load(x + i);
+        const auto yv = cr::gpu::Chunk<float, 4>::load(y + i);
+        cr::gpu::Chunk<float, 4> o;
+        for(unsigned q = 0; q < 4; ++q) o[q] = (a * xv.v[q]) + yv.v[q];
+        o.store(out + i);
+      });
+}
+// pub fn dsum(n, x: ro<f32>[n]@device) -> f32 { let s = reduce + parallel i in n yield x[i]; return s; }
+float ci_dsum(std::size_t n, const float* x) {
+  return cr::gpu::reduce_on<float>(
+      cr::gpu::here(), n, 0.0f, [] CR_DEVICE(float p, float q) { return static_cast<float>(p + q); },
+      [=] CR_DEVICE(std::size_t i) { return x[i]; });
+}
+// pub fn usum(n, x: ro<u64>[n]@device) -> u64 { let s = reduce + parallel i in n yield x[i]; return s; }
+std::uint64_t ci_usum(std::size_t n, const std::uint64_t* x) {
+  return cr::gpu::reduce_on<Sum64>(
+             cr::gpu::here(), n, Sum64{}, [] CR_DEVICE(Sum64 p, Sum64 q) { return p + q; },
+             [=] CR_DEVICE(std::size_t i) { return Sum64(x[i]); })
+      .checked();
+}
+// pub fn vmax(n, x: ro<i32>[n]@device) -> i32 { let s = reduce max parallel i in n yield x[i]; return s; }
+std::int32_t ci_vmax(std::size_t n, const std::int32_t* x) {
+  return cr::gpu::reduce_on<std::int32_t>(
+      cr::gpu::here(), n, std::int32_t(-2147483647 - 1),
+      [] CR_DEVICE(std::int32_t p, std::int32_t q) { return p < q ? q : p; },
+      [=] CR_DEVICE(std::size_t i) { return x[i]; });
+}
+// pub fn gemm(m, n, k, c: rw<f32>[cn]@device, a: ro<bf16>[an]@device, b: ro<bf16>[bn]@device)
+//   { mma_unordered(m, n, k, c, a, b); }
+void ci_gemm(std::size_t m, std::size_t n, std::size_t k, float* c, std::size_t cn, const cr::bf16* a,
+             std::size_t an, const cr::bf16* b, std::size_t bn) {
+  cr::tensor::launch<cr::bf16>(cr::gpu::here(), m, n, k, c, cn, a, an, b, bn);
+}
+}  // namespace
+
+extern "C" {
+void cf_saxpy(std::size_t n, float* out, const float* x, const float* y, float a) noexcept {
+  cr::view(out, n);
+  cr::view(x, n);
+  cr::view(y, n);
+  ci_saxpy(n, out, x, y, a);
+}
+void cf_saxpy4(std::size_t n, float* out, const float* x, const float* y, float a) noexcept {
+  cr::view(out, n);
+  cr::view(x, n);
+  cr::view(y, n);
+  ci_saxpy4(n, out, x, y, a);
+}
+void cq_saxpy(void* stream, std::size_t n, float* out, const float* x, const float* y, float a) noexcept {
+  cr::view(out, n);
+  cr::view(x, n);
+  cr::view(y, n);
+  cr::gpu::Enqueued queued(stream);
+  ci_saxpy(n, out, x, y, a);
+}
+float cf_dsum(std::size_t n, const float* x) noexcept {
+  cr::view(x, n);
+  return ci_dsum(n, x);
+}
+std::uint64_t cf_usum(std::size_t n, const std::uint64_t* x) noexcept {
+  cr::view(x, n);
+  return ci_usum(n, x);
+}
+std::int32_t cf_vmax(std::size_t n, const std::int32_t* x) noexcept {
+  cr::view(x, n);
+  return ci_vmax(n, x);
+}
+void cf_gemm(std::size_t m, std::size_t n, std::size_t k, std::size_t cn, float* c, std::size_t an,
+             const std::uint16_t* a, std::size_t bn, const std::uint16_t* b) noexcept {
+  const auto* A = reinterpret_cast<const cr::bf16*>(a);
+  const auto* B = reinterpret_cast<const cr::bf16*>(b);
+  cr::view(c, cn);
+  cr::view(A, an);
+  cr::view(B, bn);
+  cr::disjoint(c, cn, A, an);
+  cr::disjoint(c, cn, B, bn);
+  ci_gemm(m, n, k, c, cn, A, an, B, bn);
+}
+}

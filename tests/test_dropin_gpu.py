@@ -1,0 +1,89 @@
+"""The drop-in runtime headers (include/cairn_b200/runtime) under a program written the way cairnc emits one
+(tests/dropin/emitted_program.cu): the reference's own cairn_exec.hpp and cairn_reuse.hpp, unchanged, run the B200
+machine, whose regions, collectors and multiply are this project's. Each cf_/cq_ entry is held to the oracle: saxpy
+and the u64 sum bit for bit, the f32 `reduce +` (the device path's f32 fold in an unspecified order,
+docs/numerics.md) within n * 2^-24 * sum |x|, the multiply within twice its contract bound.
+
+The program is built by __graft_entry__.build() where the CAIRN reference tree is present; without the built
+library these tests are skipped, naming why."""
+
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import cairn_b200
+import inputs
+from oracle import restated
+
+pytestmark = pytest.mark.gpu
+LIB = Path(__file__).resolve().parent / "dropin" / "_build" / "libemitted.so"
+
+
+@pytest.fixture(scope="module")
+def emitted(cuda):
+    if not LIB.exists():
+        pytest.skip("tests/dropin/_build/libemitted.so is not built (it needs the CAIRN reference's headers)")
+    cairn_b200.lib()  # the program links libcairn_b200.so: load it from the tree first
+    h = C.CDLL(str(LIB))
+    z, p = C.c_size_t, C.c_void_p
+    for name, res, args in (("cf_saxpy", None, [z, p, p, p, C.c_float]), ("cf_saxpy4", None, [z, p, p, p, C.c_float]),
+                            ("cq_saxpy", None, [p, z, p, p, p, C.c_float]), ("cf_dsum", C.c_float, [z, p]),
+                            ("cf_usum", C.c_uint64, [z, p]), ("cf_vmax", C.c_int32, [z, p]),
+                            ("cf_gemm", None, [z, z, z, z, p, z, p, z, p])):
+        f = getattr(h, name)
+        f.restype, f.argtypes = res, args
+    return h
+
+
+@pytest.mark.parametrize("entry", ["cf_saxpy", "cf_saxpy4"])
+@pytest.mark.parametrize("n", [1, 1023, (1 << 22) + 3])
+def test_emitted_saxpy_regions(emitted, cuda, entry, n):
+    x_np, y_np, a = inputs.saxpy_case(n, seed=n)
+    x, y = torch.from_numpy(x_np).to(cuda), torch.from_numpy(y_np).to(cuda)
+    out = torch.empty_like(x)
+    getattr(emitted, entry)(n, out.data_ptr(), x.data_ptr(), y.data_ptr(), float(a))
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), restated.saxpy(float(a), x_np, y_np).view(np.uint32))
+
+
+def test_emitted_enqueued_saxpy_on_the_callers_stream(emitted, cuda):
+    x_np, y_np, a = inputs.saxpy_case(100_000, seed=2)
+    x, y = torch.from_numpy(x_np).to(cuda), torch.from_numpy(y_np).to(cuda)
+    out = torch.empty_like(x)
+    s = torch.cuda.Stream(cuda)
+    with torch.cuda.stream(s):
+        emitted.cq_saxpy(s.cuda_stream, x.numel(), out.data_ptr(), x.data_ptr(), y.data_ptr(), float(a))
+    s.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), restated.saxpy(float(a), x_np, y_np).view(np.uint32))
+
+
+def test_emitted_reductions(emitted, cuda):
+    rng = np.random.default_rng(4)
+    for n in (1, 300, 1_000_003):
+        x_np = rng.uniform(-1, 1, n).astype(np.float32)
+        got = emitted.cf_dsum(n, torch.from_numpy(x_np).to(cuda).data_ptr())
+        exact = float(restated.sum_f32(x_np))
+        assert abs(got - exact) <= n * 2.0**-24 * float(np.abs(x_np).sum()) + 1e-30
+        u = np.arange(n, dtype=np.uint64)
+        assert emitted.cf_usum(n, torch.from_numpy(u.view(np.int64)).to(cuda).data_ptr()) == n * (n - 1) // 2
+        v = rng.integers(-2**31, 2**31 - 1, n, dtype=np.int64).astype(np.int32)
+        assert emitted.cf_vmax(n, torch.from_numpy(v).to(cuda).data_ptr()) == int(v.max())
+
+
+@pytest.mark.parametrize("shape", [(65, 63, 33), (256, 512, 1024), (300, 264, 136)])
+def test_emitted_multiply_runs_the_tensor_cores(emitted, cuda, shape):
+    m, n, k = shape
+    c, a, b = inputs.mma_case("bf16", m, n, k, seed=m)
+    want = restated.mma("bf16", c, a, b, m, n, k)
+    ct = torch.from_numpy(c.copy()).to(cuda)
+    at = torch.from_numpy(a.view(np.int16).copy()).to(cuda)
+    bt = torch.from_numpy(b.view(np.int16).copy()).to(cuda)
+    emitted.cf_gemm(m, n, k, m * n, ct.data_ptr(), m * k, at.data_ptr(), k * n, bt.data_ptr())
+    av = np.abs(inputs.decode("bf16", a).reshape(m, k))
+    bv = np.abs(inputs.decode("bf16", b).reshape(k, n))
+    tol = 2 * (k + 1) * 2.0**-22 * (np.abs(c.reshape(m, n)) + av @ bv)
+    assert (np.abs(ct.cpu().numpy().reshape(m, n) - want.reshape(m, n)) <= tol).all()
