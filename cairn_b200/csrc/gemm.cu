@@ -332,6 +332,124 @@ __global__ void __launch_bounds__(192, 1)
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// The staged epilogue store (the pair kernel's): a warp's 32 rows x 32 columns go through a 32 x 80-byte buffer of
+// its own in shared memory. Written by rows (thread t = row t, 64 bytes: the 16-byte padding spreads the 32 rows'
+// writes over every bank) and read back by row segments (4 threads per row, 8 rows per instruction), so every global
+// store instruction writes 8 whole 64-byte row segments instead of touching 32 rows with 16 bytes each. f32 outputs
+// go through in two 16-column halves.
+// ---------------------------------------------------------------------------------------------------------------
+constexpr int STAGE_PITCH = 80;                  // bytes per staged row: 64 of data, 16 of padding
+constexpr int STAGE_BYTES = 32 * STAGE_PITCH;    // one warp's buffer
+
+__device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int col, const std::uint32_t (&r)[32],
+                                                float (&v)[32]) {
+  float bias[32];
+  if (p.bias != nullptr && col + 32 <= p.n && (reinterpret_cast<std::uintptr_t>(p.bias + col) & 15u) == 0) {
+    const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = __ldg(b4 + q);
+      bias[4 * q] = b.x;
+      bias[4 * q + 1] = b.y;
+      bias[4 * q + 2] = b.z;
+      bias[4 * q + 3] = b.w;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bias[j] = (p.bias != nullptr && col + j < p.n) ? __ldg(p.bias + col + j) : 0.0f;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    float x = __fadd_rn(__uint_as_float(r[j]), bias[j]);
+    if (p.act == ACT_RELU) x = x < 0.0f ? 0.0f : x;
+    v[j] = x;
+  }
+  if (p.mask != nullptr && row < p.m) {
+    const std::uint16_t* mrow = p.mask + static_cast<std::size_t>(row) * p.n + col;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col + j < p.n && !(__uint_as_float(static_cast<std::uint32_t>(__ldg(mrow + j)) << 16) > 0.0f)) v[j] = 0.0f;
+  }
+}
+
+// Stores the warp's 32 x 32 chunk whose first row is row0 (this thread holds row row0 + lane) at column col.
+__device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, int col, const std::uint32_t (&r)[32],
+                                                   std::uint8_t* stage, int lane) {
+  const int seg = lane & 3, sub = lane >> 2;  // read-back: 4 threads per row (16 bytes each), 8 rows per pass
+  if (p.out_kind == OUT_BF16) {
+    float v[32];
+    epilogue_values(p, row0 + lane, col, r, v);
+    uint4* mine = reinterpret_cast<uint4*>(stage + lane * STAGE_PITCH);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint4 w;
+      __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
+      __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
+      __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
+      __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
+      std::memcpy(&w.x, &h0, 4);
+      std::memcpy(&w.y, &h1, 4);
+      std::memcpy(&w.z, &h2, 4);
+      std::memcpy(&w.w, &h3, 4);
+      mine[q] = w;
+    }
+    __syncwarp();
+#pragma unroll
+    for (int pass = 0; pass < 4; ++pass) {
+      const int rr = pass * 8 + sub, row = row0 + rr, c0 = col + seg * 8;
+      const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * STAGE_PITCH + seg * 16);
+      if (row < p.m) {
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + static_cast<std::size_t>(row) * p.n + c0;
+        if (p.vec && c0 + 8 <= p.n) {
+          *reinterpret_cast<uint4*>(dst) = w;
+        } else {
+          const std::uint16_t* h = reinterpret_cast<const std::uint16_t*>(&w);
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (c0 + j < p.n) reinterpret_cast<std::uint16_t*>(dst)[j] = h[j];
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    const bool acc = p.out_kind == OUT_ACC_F32;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      float4* mine = reinterpret_cast<float4*>(stage + lane * STAGE_PITCH);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        mine[q] = make_float4(__uint_as_float(r[16 * half + 4 * q]), __uint_as_float(r[16 * half + 4 * q + 1]),
+                              __uint_as_float(r[16 * half + 4 * q + 2]), __uint_as_float(r[16 * half + 4 * q + 3]));
+      __syncwarp();
+#pragma unroll
+      for (int pass = 0; pass < 4; ++pass) {
+        const int rr = pass * 8 + sub, row = row0 + rr, c0 = col + 16 * half + seg * 4;
+        float4 w = *reinterpret_cast<const float4*>(stage + rr * STAGE_PITCH + seg * 16);
+        if (row < p.m) {
+          float* dst = static_cast<float*>(p.out) + static_cast<std::size_t>(row) * p.n + c0;
+          if (p.vec && c0 + 4 <= p.n) {
+            if (acc) {
+              const float4 old = *reinterpret_cast<const float4*>(dst);
+              w.x = __fadd_rn(old.x, w.x);
+              w.y = __fadd_rn(old.y, w.y);
+              w.z = __fadd_rn(old.z, w.z);
+              w.w = __fadd_rn(old.w, w.w);
+            }
+            *reinterpret_cast<float4*>(dst) = w;
+          } else {
+            const float e[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              if (c0 + j < p.n) dst[j] = acc ? __fadd_rn(dst[j], e[j]) : e[j];
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // The two-SM multiply: a cluster of two CTAs (a pair) computes a 256 x (256 G) tile with tcgen05.mma.cta_group::2,
 // G = 1 or 2 column groups of 256. Each CTA stages its own half of the operands at the same shared-memory offsets:
 // rows [128 r, 128 r + 128) of the tile's A, and in each column group g the columns [256 g + 128 r, + 128) of B,
@@ -356,7 +474,7 @@ template <int G> struct PairShape {
   static constexpr int EPI_WARPS = 8;                               // two warps per TMEM lane quarter
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int TILE_N = G * PAIR_BN;
-  static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_HALF) + 256;
+  static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_HALF) + 256 + EPI_WARPS * STAGE_BYTES;
 };
 
 template <int FMT, int G>
@@ -386,6 +504,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
   std::uint64_t* drain = tempty + 2;
   std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(drain + 1);
   volatile std::uint32_t* abort_flag = tmem_slot + 1;
+  std::uint8_t* epi_stage = reinterpret_cast<std::uint8_t*>(bars) + 256;  // EPI_WARPS buffers of STAGE_BYTES
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const std::uint32_t rank = cluster_rank();
@@ -520,8 +639,9 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       tc_fence_after();
       int mb, nb;
       tile_of(t, num_m, num_n, mb, nb);
-      const int row = mb * 2 * HALF + static_cast<int>(rank) * HALF + quarter * 32 + lane;
+      const int row0 = mb * 2 * HALF + static_cast<int>(rank) * HALF + quarter * 32;
       const std::uint32_t t_row = tmem_base + (static_cast<std::uint32_t>(quarter * 32) << 16) + acc * PAIR_BN;
+      std::uint8_t* stage = epi_stage + (warp - 2) * STAGE_BYTES;
 #pragma unroll 1
       for (int c = col0; c < col0 + COLS_PER_WARP; c += 32) {
         std::uint32_t r[32];
@@ -532,7 +652,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
         }
-        store_chunk<FMT>(p, row, nb * S::TILE_N + c, r);
+        store_chunk_staged(p, row0, nb * S::TILE_N + c, r, stage, lane);
       }
     }
   }
