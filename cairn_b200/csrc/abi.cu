@@ -73,11 +73,14 @@ struct Scratch {
 };
 struct Arena {
   Scratch slot[MAX_DEVICES];
+  Scratch gemm[MAX_DEVICES];           // the multiply's stream-K workspace, grown to the largest request
+  std::uint32_t arrivals[MAX_DEVICES] = {};  // grid-barrier arrivals every launch on gemm[d] has added so far
   ~Arena() {
-    for (Scratch& s : slot) {
-      if (s.ptr) cudaFree(s.ptr);  // errors at process exit (runtime already unloaded) are ignored
-      if (s.last) cudaEventDestroy(s.last);
-    }
+    for (Scratch* set : {slot, gemm})
+      for (int d = 0; d < MAX_DEVICES; ++d) {
+        if (set[d].ptr) cudaFree(set[d].ptr);  // errors at process exit (runtime already unloaded) are ignored
+        if (set[d].last) cudaEventDestroy(set[d].last);
+      }
   }
 };
 thread_local Arena t_arena;
@@ -106,6 +109,42 @@ int release(cudaStream_t stream) {
   s.used = true;
   return CAIRN_B200_OK;
 }
+// Lends the thread's multiply workspace on the current device, grown to `bytes` if it is smaller (the growth waits
+// for the workspace's last user, frees it and allocates a zeroed one: its arrival counter must start at zero).
+// Ordered after its previous user's stream like the reduction scratch. `base` is the counter's value when the
+// launch starts: the arrivals of every earlier launch on this workspace.
+int acquire_gemm(cudaStream_t stream, std::size_t bytes, void** out, std::uint32_t* base) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CAIRN_B200_ERR_CUDA;
+  Scratch& s = t_arena.gemm[dev];
+  if (!s.last && cudaEventCreateWithFlags(&s.last, cudaEventDisableTiming) != cudaSuccess) return CAIRN_B200_ERR_CUDA;
+  if (s.bytes < bytes) {
+    if (s.used && cudaEventSynchronize(s.last) != cudaSuccess) return CAIRN_B200_ERR_CUDA;
+    if (s.ptr) cudaFree(s.ptr);
+    s.ptr = nullptr;
+    s.bytes = 0;
+    s.used = false;
+    if (cudaMalloc(&s.ptr, bytes) != cudaSuccess) return CAIRN_B200_ERR_CUDA;
+    if (cudaMemset(s.ptr, 0, bytes) != cudaSuccess) return CAIRN_B200_ERR_CUDA;
+    s.bytes = bytes;
+    t_arena.arrivals[dev] = 0;
+  }
+  if (s.used && cudaStreamWaitEvent(stream, s.last, 0) != cudaSuccess) return CAIRN_B200_ERR_CUDA;
+  *out = s.ptr;
+  *base = t_arena.arrivals[dev];
+  return CAIRN_B200_OK;
+}
+// After a launch on the workspace: the next user follows it, and its arrivals (when it was launched) are counted.
+int release_gemm(cudaStream_t stream, std::uint32_t added) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return CAIRN_B200_ERR_CUDA;
+  Scratch& s = t_arena.gemm[dev];
+  t_arena.arrivals[dev] += added;  // wraps modulo 2^32, as the kernel's comparison does
+  if (cudaEventRecord(s.last, stream) != cudaSuccess) return CAIRN_B200_ERR_CUDA;
+  s.used = true;
+  return CAIRN_B200_OK;
+}
+
 // The cell after the reduction scratch that a _host entry reduces into before copying it back.
 void* result_cell(const Device& d, void* scratch) {
   return static_cast<char*>(scratch) + reduce_scratch_bytes(d.sms);
@@ -160,8 +199,14 @@ int gemm_entry(cudaStream_t stream, int fmt, std::size_t m, std::size_t n, std::
   int status;
   const Device* d = current(&status);
   if (!d) return status;
-  GemmArgs g{fmt, m, n, k, a, trans_a, b, trans_b, out, out_kind, biased ? bias : nullptr, act, mask};
-  return cuda_status(gemm_launch(g, stream, d->sms, d->fault));
+  GemmArgs g{fmt, m, n, k, a, trans_a, b, trans_b, out, out_kind, biased ? bias : nullptr, act, mask, nullptr, 0};
+  std::uint32_t arrivals = 0;
+  const std::size_t ws_bytes = gemm_workspace_bytes(g, d->sms, &arrivals);
+  if (ws_bytes == 0) return cuda_status(gemm_launch(g, stream, d->sms, d->fault));
+  if ((status = acquire_gemm(stream, ws_bytes, &g.ws, &g.epoch)) != CAIRN_B200_OK) return status;
+  const cudaError_t e = gemm_launch(g, stream, d->sms, d->fault);
+  const int r = release_gemm(stream, e == cudaSuccess ? arrivals : 0u);
+  return e != cudaSuccess ? CAIRN_B200_ERR_CUDA : r;
 }
 
 int mma_entry(void* stream, int fmt, std::size_t m, std::size_t n, std::size_t k, float* c, std::size_t cn,

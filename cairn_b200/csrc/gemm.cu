@@ -55,6 +55,10 @@ struct TcParams {
   const std::uint16_t* mask;  // OUT_BF16 only: keep an output where this m x n bf16 array is > 0, else 0
   int vec;        // every output row starts on 16 bytes and holds whole 16-byte groups
   std::uint32_t* fault;
+  int streamk;            // split the tiles' k-blocks evenly over the pairs (pair kernel only)
+  float* ws;              // stream-K partials: two slots per CTA of every pair
+  std::uint32_t* flags;   // stream-K grid barrier: the count of CTAs that have written their partials
+  std::uint32_t epoch;    // the count's value when this launch starts
 };
 
 constexpr int BM = 128;              // rows of a tile: the MMA's M, one TMEM lane per row
@@ -450,6 +454,55 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// A pair's work, as segments (tile, first k-block, end k-block). Data-parallel: whole tiles pair, pair + pairs, ...
+// Stream-K: the tiles x k-blocks units cut into `pairs` contiguous ranges of equal length, so every pair does the
+// same amount of MMA work however the tile count divides. A range that starts inside a tile begins with that
+// tile's later k-blocks (a contributor: it publishes an f32 partial); one that ends inside a tile ends with that
+// tile's first k-blocks (the finisher: it adds the contributors' partials and writes the tile). A pair contributes at
+// most once, first, and finishes at most once, last, so a finisher waits only for work its contributors did at the
+// start of the launch.
+// ---------------------------------------------------------------------------------------------------------------
+// Where a 32 x 32 block of a split tile's partial sum sits in a CTA's workspace slot, in float4 units: block (w, ci)
+// of epilogue warp w, chunk ci, holds 8 rows of 32 float4 (row e: values 4e .. 4e + 3 of every lane), so each warp
+// store and load covers 512 contiguous bytes.
+__device__ __forceinline__ std::size_t partial_cell(int w, int ci, int chunks) {
+  return static_cast<std::size_t>(w * chunks + ci) * 256;
+}
+
+struct PairWork {
+  long long u, u_end;  // stream-K: this pair's units
+  int t, tiles, pairs, num_kb;
+  bool sk;
+  __device__ PairWork(int pair, int pairs_, int tiles_, int num_kb_, bool streamk)
+      : t(pair), tiles(tiles_), pairs(pairs_), num_kb(num_kb_), sk(streamk) {
+    const long long units = static_cast<long long>(tiles_) * num_kb_;
+    u = units * pair / pairs_;
+    u_end = units * (pair + 1) / pairs_;
+  }
+  __device__ bool next(int& tile, int& kb0, int& kb1) {
+    if (!sk) {
+      if (t >= tiles) return false;
+      tile = t;
+      kb0 = 0;
+      kb1 = num_kb;
+      t += pairs;
+      return true;
+    }
+    if (u >= u_end) return false;
+    tile = static_cast<int>(u / num_kb);
+    kb0 = static_cast<int>(u % num_kb);
+    const long long left = u_end - u;
+    kb1 = left < num_kb - kb0 ? kb0 + static_cast<int>(left) : num_kb;
+    u += kb1 - kb0;
+    return true;
+  }
+  // The first unit of pair q's range.
+  __device__ long long start_of(int q) const {
+    return static_cast<long long>(tiles) * num_kb * q / pairs;
+  }
+};
+
+// ---------------------------------------------------------------------------------------------------------------
 // The two-SM multiply: a cluster of two CTAs (a pair) computes a 256 x (256 G) tile with tcgen05.mma.cta_group::2,
 // G = 1 or 2 column groups of 256. Each CTA stages its own half of the operands at the same shared-memory offsets:
 // rows [128 r, 128 r + 128) of the tile's A, and in each column group g the columns [256 g + 128 r, + 128) of B,
@@ -502,7 +555,8 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
   std::uint64_t* tfull = bars + 2 * STAGES;
   std::uint64_t* tempty = tfull + 2;
   std::uint64_t* drain = tempty + 2;
-  std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(drain + 1);
+  std::uint64_t* published = drain + 1;  // every epilogue warp of this CTA has written its stream-K partial
+  std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(published + 1);
   volatile std::uint32_t* abort_flag = tmem_slot + 1;
   std::uint8_t* epi_stage = reinterpret_cast<std::uint8_t*>(bars) + 256;  // EPI_WARPS buffers of STAGE_BYTES
 
@@ -523,6 +577,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       mbar_init(&tempty[a], 2 * S::EPI_WARPS);
     }
     mbar_init(drain, 1);
+    mbar_init(published, S::EPI_WARPS);
     *abort_flag = 0u;
     fence_barrier_init();
   }
@@ -540,12 +595,14 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       tma_prefetch_desc(&tm_a);
       tma_prefetch_desc(&tm_b);
       std::uint32_t stage = 0, phase = 0;
-      for (int t = pair; t < tiles; t += pairs) {
+      PairWork work(pair, pairs, tiles, num_kb, p.streamk != 0);
+      int t, kb_begin, kb_end;
+      while (work.next(t, kb_begin, kb_end)) {
         int mb, nb;
         tile_of(t, num_m, num_n, mb, nb);
         const int m0 = mb * 2 * HALF + static_cast<int>(rank) * HALF;  // this CTA's rows of A
         const int n_tile = nb * S::TILE_N;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.fault, FAULT_WAIT_EMPTY)) goto producer_done;
           const std::uint32_t leader_full = cluster_addr(&full[stage], 0);
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2u * (A_STAGE + S::B_HALF));
@@ -591,13 +648,15 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       const std::uint32_t b_sbo = b_layout == LAYOUT_SW128_32B ? 512u : 1024u;
       const std::uint32_t a_lbo = p.a_mn ? CH * SLICE : 16u, b_lbo = p.b_k ? 16u : CH * SLICE;
       std::uint32_t stage = 0, phase = 0, it = 0;
-      for (int t = pair; t < tiles; t += pairs, ++it) {
+      PairWork work(pair, pairs, tiles, num_kb, p.streamk != 0);
+      int t, kb_begin, kb_end;
+      for (; work.next(t, kb_begin, kb_end); ++it) {
         const std::uint32_t acc = S::ACCS == 2 ? (it & 1u) : 0u;
         const std::uint32_t acc_phase = S::ACCS == 2 ? ((it >> 1) & 1u) : (it & 1u);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.fault, FAULT_WAIT_TEMPTY)) goto mma_done;
         tc_fence_after();
         const std::uint32_t d_tmem = tmem_base + acc * PAIR_BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!mbar_wait(&full[stage], phase, abort_flag, p.fault, FAULT_WAIT_FULL)) goto mma_done;
           tc_fence_after();
           const std::uint32_t a_addr = smem_u32(a_smem + stage * A_STAGE);
@@ -611,7 +670,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
             for (int g = 0; g < G; ++g)
               umma_pair<F::kind>(d_tmem + g * PAIR_BN, a_desc,
                                  sdesc(b_addr + g * GROUP_BYTES + b_off, b_lbo, b_sbo, b_layout), idesc,
-                                 (kb | kk) != 0 ? 1u : 0u);
+                                 (kb != kb_begin || kk != 0) ? 1u : 0u);
           }
           tc_commit_pair(cluster_addr(&empty[stage], 0));
           tc_commit_pair(cluster_addr(&empty[stage], 1));
@@ -630,9 +689,15 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
     __syncwarp();
   } else {
     const int quarter = warp & 3;                       // TMEM lanes 32 * (warp id % 4) .. + 31
-    const int col0 = ((warp - 2) / 4) * COLS_PER_WARP;  // this warp's half of the tile's columns
+    const int ew = warp - 2;                            // epilogue warp 0..EPI_WARPS-1
+    const int col0 = (ew / 4) * COLS_PER_WARP;          // this warp's half of the tile's columns
+    constexpr int CHUNKS = COLS_PER_WARP / 32;
+    constexpr std::size_t SLOT = static_cast<std::size_t>(S::EPI_WARPS) * CHUNKS * 32 * 32;  // floats per slot
+    std::uint8_t* stage = epi_stage + ew * STAGE_BYTES;
     std::uint32_t it = 0;
-    for (int t = pair; t < tiles; t += pairs, ++it) {
+    PairWork work(pair, pairs, tiles, num_kb, p.streamk != 0);
+    int t, kb_begin, kb_end;
+    for (; work.next(t, kb_begin, kb_end); ++it) {
       const std::uint32_t acc = S::ACCS == 2 ? (it & 1u) : 0u;
       const std::uint32_t acc_phase = S::ACCS == 2 ? ((it >> 1) & 1u) : (it & 1u);
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.fault, FAULT_WAIT_TFULL)) break;
@@ -641,18 +706,98 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       tile_of(t, num_m, num_n, mb, nb);
       const int row0 = mb * 2 * HALF + static_cast<int>(rank) * HALF + quarter * 32;
       const std::uint32_t t_row = tmem_base + (static_cast<std::uint32_t>(quarter * 32) << 16) + acc * PAIR_BN;
-      std::uint8_t* stage = epi_stage + (warp - 2) * STAGE_BYTES;
+      // A segment holding part of a tile's k-blocks leaves its raw f32 sum in one of this CTA's two slots (slot 0
+      // for the pair's first segment, slot 1 for its last); the fix-up after the grid barrier adds the parts.
+      const bool split = kb_begin > 0 || kb_end < num_kb;
+      float* slot = p.ws + static_cast<std::size_t>(2 * (2 * pair + static_cast<int>(rank)) + (it ? 1 : 0)) * SLOT;
 #pragma unroll 1
-      for (int c = col0; c < col0 + COLS_PER_WARP; c += 32) {
+      for (int ci = 0; ci < CHUNKS; ++ci) {
+        const int c = col0 + ci * 32;
         std::uint32_t r[32];
         tmem_ld_32x32b_x32(t_row + c, r);
         tmem_wait_ld();
-        if (c + 32 == col0 + COLS_PER_WARP) {  // this warp's part of the accumulator is in registers
+        if (ci + 1 == CHUNKS) {  // this warp's part of the accumulator is in registers
           tc_fence_before();
           __syncwarp();
           if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
         }
-        store_chunk_staged(p, row0, nb * S::TILE_N + c, r, stage, lane);
+        if (split) {
+          float4* dst = reinterpret_cast<float4*>(slot) + partial_cell(ew, ci, CHUNKS) + lane;
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            __stcg(dst + q * 32, make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                             __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
+        } else {
+          store_chunk_staged(p, row0, nb * S::TILE_N + c, r, stage, lane);
+        }
+      }
+    }
+    if (p.streamk) {
+      // The grid barrier: once every CTA's epilogue warps have written their partials, each CTA adds one arrival to
+      // the workspace's counter; the fix-up starts when all gridDim.x arrivals of this launch are in (the host
+      // passes the count before it as p.epoch). All CTAs are resident, so the wait ends; it is bounded all the same.
+      __threadfence();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(published);
+      if (ew == 0 && lane == 0) {
+        mbar_wait(published, 0u, abort_flag, p.fault, FAULT_WAIT_PEER);
+        __threadfence();
+        atomicAdd(p.flags, 1u);
+      }
+      if (lane == 0) {
+        const std::uint32_t target = p.epoch + gridDim.x;
+        const std::uint64_t start = globaltimer();
+        while (static_cast<int>(ld_acquire_gpu(p.flags) - target) < 0) {
+          if (*abort_flag) break;
+          if (globaltimer() - start > WAIT_LIMIT_NS) {
+            atomicOr(p.fault, static_cast<std::uint32_t>(FAULT_WAIT_PEER));
+            *abort_flag = 1u;
+            break;
+          }
+        }
+      }
+      __syncwarp();
+      // The fix-up: the grid's epilogue warps take (tile, rank, 32 x 32 block) items in turn. A tile that one pair
+      // computed whole was stored already; a split tile's block is the sum of its parts in pair order, then the
+      // epilogue.
+      const long long units = static_cast<long long>(tiles) * num_kb;
+      const int per_rank = S::EPI_WARPS * CHUNKS, per_tile = 2 * per_rank;
+      const int items = tiles * per_tile;
+      for (int item = blockIdx.x * S::EPI_WARPS + ew; item < items && !*abort_flag;
+           item += gridDim.x * S::EPI_WARPS) {
+        const int tt = item / per_tile, rr = (item % per_tile) / per_rank, wc = item % per_rank;
+        const int w = wc / CHUNKS, ci = wc % CHUNKS;
+        const long long lo = static_cast<long long>(tt) * num_kb, hi = lo + num_kb;
+        int q = static_cast<int>(lo * pairs / units);  // the pair whose range holds k-block 0 of the tile
+        while (q + 1 < pairs && work.start_of(q + 1) <= lo) ++q;
+        while (q > 0 && work.start_of(q) > lo) --q;
+        if (work.start_of(q + 1) >= hi) continue;  // one pair's range holds the whole tile
+        std::uint32_t r[32];
+        for (int qq = q; qq < pairs && work.start_of(qq) < hi; ++qq) {
+          const int which = work.start_of(qq) >= lo ? 0 : 1;  // the tile is this pair's first segment, or its last
+          const float* part = p.ws + static_cast<std::size_t>(2 * (2 * qq + rr) + which) * SLOT;
+          const float4* src = reinterpret_cast<const float4*>(part) + partial_cell(w, ci, CHUNKS) + lane;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            const float4 v = __ldcg(src + e * 32);
+            if (qq == q) {
+              r[4 * e] = __float_as_uint(v.x);
+              r[4 * e + 1] = __float_as_uint(v.y);
+              r[4 * e + 2] = __float_as_uint(v.z);
+              r[4 * e + 3] = __float_as_uint(v.w);
+            } else {
+              r[4 * e] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * e]), v.x));
+              r[4 * e + 1] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * e + 1]), v.y));
+              r[4 * e + 2] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * e + 2]), v.z));
+              r[4 * e + 3] = __float_as_uint(__fadd_rn(__uint_as_float(r[4 * e + 3]), v.w));
+            }
+          }
+        }
+        int mb, nb;
+        tile_of(tt, num_m, num_n, mb, nb);
+        const int w_quarter = (w + 2) & 3;  // epilogue warp w is warp w + 2: its TMEM lane quarter
+        store_chunk_staged(p, mb * 2 * HALF + rr * HALF + w_quarter * 32,
+                           nb * S::TILE_N + (w / 4) * COLS_PER_WARP + ci * 32, r, stage, lane);
       }
     }
   }
@@ -829,6 +974,35 @@ int pair_path(const GemmArgs& g) {
   return g.n >= 512 ? 2 : 1;
 }
 
+// How the pair kernel covers `tiles` tiles of `num_kb` k-blocks with at most `most` resident pairs. Data-parallel
+// (each pair takes whole tiles in turn) unless the tiles would leave most pairs idle while each has a long k loop:
+// then stream-K spreads the k-blocks of all tiles evenly over more pairs, at least STREAMK_MIN_KB each, and the pairs
+// that share a tile add their partial sums through a workspace. Measured on a B200 (4096^3 bf16): with as many tiles
+// as pairs or more, splitting k costs more than the last wave's idle pairs do (DRAM reads 161 MB against 78 MB, L2
+// hits 70 % against 79 %: pairs that share a panel no longer read it at the same time), so it is not used there.
+// CAIRN_B200_STREAMK=0 or 1 pins the choice (1 splits whenever there is more than one pair).
+constexpr int STREAMK_MIN_KB = 32;
+struct PairPlan {
+  int pairs;
+  bool streamk;
+};
+PairPlan pair_plan(int tiles, int num_kb, int resident, int sms) {
+  static const int pinned = [] {
+    const char* v = std::getenv("CAIRN_B200_STREAMK");
+    return (v && (v[0] == '0' || v[0] == '1')) ? v[0] - '0' : -1;
+  }();
+  const int most = resident > 0 ? resident : sms / 2;
+  const PairPlan dp{tiles < most ? tiles : most, false};
+  const bool want = pinned >= 0 ? pinned == 1 : (2 * tiles <= most && num_kb >= 2 * STREAMK_MIN_KB);
+  if (!want || resident <= 0) return dp;  // stream-K's finishing pairs wait for the others: all must be resident
+  const long long units = static_cast<long long>(tiles) * num_kb;
+  long long pairs = units / STREAMK_MIN_KB;
+  pairs = pairs > tiles ? pairs : tiles;
+  pairs = pairs < most ? pairs : most;
+  if (pairs < 2) return dp;
+  return PairPlan{static_cast<int>(pairs), true};
+}
+
 template <int FMT, int BN>
 cudaError_t launch_tc(const GemmArgs& g, const TcParams& p, cudaStream_t stream, int sms) {
   using S = Shape<BN>;
@@ -857,6 +1031,54 @@ cudaError_t launch_tc(const GemmArgs& g, const TcParams& p, cudaStream_t stream,
   return cudaGetLastError();
 }
 
+// The pair kernel's dynamic shared memory, set once per device and instantiation before its first launch.
+template <int FMT, int G> cudaError_t configure_pair() {
+  static std::atomic<std::uint64_t> configured{0};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const std::uint64_t bit = 1ull << (dev & 63);
+  if (configured.load(std::memory_order_acquire) & bit) return cudaSuccess;
+  e = cudaFuncSetAttribute(tc_gemm_pair_kernel<FMT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           PairShape<G>::SMEM);
+  if (e != cudaSuccess) return e;
+  configured.fetch_or(bit, std::memory_order_acq_rel);
+  return cudaSuccess;
+}
+
+// How many pairs (two-CTA clusters) of the G-group kernel the device holds at once: clusters must fit inside one
+// GPC, so this can be below sms / 2. Every storage format's instantiation has the same shared memory and threads,
+// so the bf16 one answers for all. Cached per device; 0 when the query fails (stream-K is then not used, since its
+// finishing CTAs wait for the others and so need them all resident).
+template <int G> int resident_pairs(int sms) {
+  static std::atomic<int> cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  const int known = cached[dev & 63].load(std::memory_order_acquire);
+  if (known) return known;
+  if (configure_pair<FMT_BF16, G>() != cudaSuccess) return 0;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(sms, 1, 1);
+  cfg.blockDim = dim3(PairShape<G>::THREADS, 1, 1);
+  cfg.dynamicSmemBytes = PairShape<G>::SMEM;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int clusters = 0;
+  if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_pair_kernel<FMT_BF16, G>, &cfg) != cudaSuccess ||
+      clusters <= 0) {
+    cudaGetLastError();  // leave no sticky error behind for the launch to report
+    return 0;
+  }
+  const int pairs = clusters < sms / 2 ? clusters : sms / 2;
+  cached[dev & 63].store(pairs, std::memory_order_release);
+  return pairs;
+}
+
 template <int FMT, int G>
 cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t stream, int sms) {
   using S = PairShape<G>;
@@ -869,18 +1091,18 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   const bool ok_b = g.trans_b ? encode(&tb, FMT, g.b, g.k, g.n, es, CH, HALF, false)
                               : encode(&tb, FMT, g.b, g.n, g.k, es, CH, CH, true);
   if (!ok_a || !ok_b) return cudaErrorInvalidValue;
-  static std::atomic<std::uint64_t> configured{0};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  cudaError_t e = configure_pair<FMT, G>();
   if (e != cudaSuccess) return e;
-  const std::uint64_t bit = 1ull << (dev & 63);
-  if (!(configured.load(std::memory_order_acquire) & bit)) {
-    e = cudaFuncSetAttribute(tc_gemm_pair_kernel<FMT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM);
-    if (e != cudaSuccess) return e;
-    configured.fetch_or(bit, std::memory_order_acq_rel);
-  }
   const int tiles = ((p.m + 2 * HALF - 1) / (2 * HALF)) * ((p.n + S::TILE_N - 1) / S::TILE_N);
-  const int pairs = tiles < sms / 2 ? tiles : sms / 2;
+  const int num_kb = (p.k + CH - 1) / CH;
+  PairPlan plan = pair_plan(tiles, num_kb, resident_pairs<G>(sms), sms);
+  if (plan.streamk && g.ws == nullptr) plan = pair_plan(tiles, num_kb, 0, sms);  // no workspace: data-parallel
+  const int pairs = plan.pairs;
+  TcParams q = p;
+  q.streamk = plan.streamk;
+  q.flags = static_cast<std::uint32_t*>(g.ws);  // the workspace: the barrier's arrival counter, then the slots
+  q.ws = g.ws ? reinterpret_cast<float*>(static_cast<char*>(g.ws) + 256) : nullptr;
+  q.epoch = g.epoch;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(S::THREADS, 1, 1);
@@ -893,7 +1115,7 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G>, ta, tb, p);
+  e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G>, ta, tb, q);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
@@ -928,6 +1150,23 @@ bool tensor_path_ok(const GemmArgs& g) {
   if (a_row % 16 || b_row % 16) return false;
   const std::uint64_t lim = 1ull << 31;
   return g.m < lim && g.n < lim && g.k < lim;
+}
+
+std::size_t gemm_workspace_bytes(const GemmArgs& g, int sms, std::uint32_t* arrivals) {
+  *arrivals = 0;
+  if (!tensor_path_ok(g)) return 0;
+  const int G = pair_path(g);
+  if (G == 0) return 0;
+  const int tile_n = G * PAIR_BN;
+  const std::uint64_t tiles64 = ((g.m + 255) / 256) * ((g.n + tile_n - 1) / tile_n);
+  const std::uint64_t ch = SLICE / esize_of(g.fmt);
+  const PairPlan plan = pair_plan(static_cast<int>(tiles64), static_cast<int>((g.k + ch - 1) / ch),
+                                  G == 1 ? resident_pairs<1>(sms) : resident_pairs<2>(sms), sms);
+  if (!plan.streamk) return 0;
+  *arrivals = 2u * static_cast<std::uint32_t>(plan.pairs);
+  // the arrival counter (256 bytes), then two slots per CTA of EPI_WARPS x (tile_n / 64) blocks of 32 x 32 floats
+  const std::size_t slot = static_cast<std::size_t>(8) * (tile_n / 64) * 32 * 32 * sizeof(float);
+  return 256 + static_cast<std::size_t>(plan.pairs) * 2 * 2 * slot;
 }
 
 cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream, int sms, std::uint32_t* fault) {

@@ -23,7 +23,17 @@ struct GemmArgs {
   const float* bias;
   int act;
   const std::uint16_t* mask;  // OUT_BF16: zero the outputs where this bf16 m x n array is not > 0 (may be null)
+  // Stream-K workspace, filled in by gemm_launch's caller when gemm_workspace_bytes asks for one: a grid barrier's
+  // arrival counter (zero when the workspace was allocated) and the split tiles' f32 partials; `epoch` is the count
+  // of arrivals every earlier launch on this workspace added.
+  void* ws;
+  std::uint32_t epoch;
 };
+
+// Bytes of stream-K workspace the product needs on a device with `sms` SMs (0: no tile is split); the flags sit at
+// the end, and a fresh workspace must hold zeros there.
+// The stream-K workspace a launch of g needs (0: none), and how many arrivals it adds to the workspace's counter.
+std::size_t gemm_workspace_bytes(const GemmArgs& g, int sms, std::uint32_t* arrivals);
 
 // True when the tensor-core path reads both operands through TMA (otherwise the SIMT tile kernel runs).
 bool tensor_path_ok(const GemmArgs& g);

@@ -19,7 +19,22 @@ enum Fault : std::uint32_t {
   FAULT_WAIT_TFULL = 1u << 2,   // an epilogue warp waited for an accumulator
   FAULT_WAIT_TEMPTY = 1u << 3,  // the MMA issuer waited for an accumulator to be drained
   FAULT_DRAIN = 1u << 4,        // the exit path waited for copies or MMAs still in flight
+  FAULT_WAIT_PEER = 1u << 5,    // a stream-K CTA waited at the grid barrier for the others' partials
 };
+
+// A flag another CTA raises: read with acquire ordering at GPU scope, raised with release ordering.
+__device__ __forceinline__ std::uint32_t ld_acquire_gpu(const std::uint32_t* p) {
+  std::uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(std::uint32_t* p, std::uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// A barrier among `count` threads of the block (a multiple of 32) on hardware barrier `id` (1..15).
+__device__ __forceinline__ void named_barrier(std::uint32_t id, std::uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 
 __device__ __forceinline__ std::uint64_t globaltimer() {
   std::uint64_t t;
