@@ -6,7 +6,7 @@
 // The machine keeps every member the context and the operations call (runtime/cairn_gpu.hpp:47-125), each one CUDA
 // call as before: streams, events, allocation, copies, and the region launchers, which now come from this
 // directory's cairn_kernels.hpp (persistent, device-sized grids). Its `reduce` is this project's own kernel instead
-// of CUB's (defined in this directory's cairn_cub.hpp); the scans stay on CUB.
+// of CUB's, and so are its scans (defined in this directory's cairn_cub.hpp).
 #pragma once
 #if !defined(CAIRN_EMULATE)
 #include <cstdio>

@@ -1,7 +1,7 @@
 // A CAIRN device library in the form cairnc emits it (compiler/lower/codegen.py:438-446 for the checked cf_ entries,
 // compiler/lower/header.py:230-247 for the enqueued cq_ entries, compiler/lower/region_lowering.py:122-183 and
 // compiler/device/tensor.py:69-82 for the bodies): every function's body calls only the runtime's templates,
-// cr::gpu::run, cr::gpu::run_vector, cr::gpu::reduce_on and cr::tensor::launch. It is built against the CAIRN
+// cr::gpu::run, cr::gpu::run_vector, cr::gpu::reduce_on, cr::gpu::scan_on, cr::gpu::compact_on and cr::tensor::launch. It is built against the CAIRN
 // runtime headers with include/cairn_b200/runtime ahead of them on the include path (tests/dropin/build_emitted.py),
 // so the same source runs on the B200 machine and libcairn_b200.so. Test input of tests/test_dropin_gpu.py.
 #include <cstddef>
@@ -59,6 +59,43 @@ void ci_gemm(std::size_t m, std::size_t n, std::size_t k, float* c, std::size_t 
              std::size_t an, const cr::bf16* b, std::size_t bn) {
   cr::tensor::launch<cr::bf16>(cr::gpu::here(), m, n, k, c, cn, a, an, b, bn);
 }
+// pub fn prefix(n, out: rw<u64>[n]@device, x: ro<u64>[n]@device) -> u64
+//   { let s = scan + parallel i in n yield x[i] into out; return s; }
+std::uint64_t ci_prefix(std::size_t n, std::uint64_t* out, const std::uint64_t* x) {
+  return cr::gpu::scan_on<false, Sum64>(
+             cr::gpu::here(), out, n, Sum64{}, [] CR_DEVICE(Sum64 p, Sum64 q) { return p + q; },
+             [=] CR_DEVICE(std::size_t i) { return Sum64(x[i]); })
+      .checked();
+}
+// pub fn wprefix(n, out: rw<u32>[n]@device, x: ro<u32>[n]@device) -> u32
+//   { let s = scan add_wrap parallel i in n yield x[i] into out; return s; }
+std::uint32_t ci_wprefix(std::size_t n, std::uint32_t* out, const std::uint32_t* x) {
+  return cr::gpu::scan_on<false, std::uint32_t>(
+      cr::gpu::here(), out, n, 0u, [] CR_DEVICE(std::uint32_t p, std::uint32_t q) { return cr::add_wrap(p, q); },
+      [=] CR_DEVICE(std::size_t i) { return x[i]; });
+}
+// pub fn runmax(n, out: rw<i32>[n]@device, x: ro<i32>[n]@device) -> i32
+//   { let s = scan exclusive max parallel i in n yield x[i] into out; return s; }
+std::int32_t ci_runmax(std::size_t n, std::int32_t* out, const std::int32_t* x) {
+  return cr::gpu::scan_on<true, std::int32_t>(
+      cr::gpu::here(), out, n, std::int32_t(-2147483647 - 1),
+      [] CR_DEVICE(std::int32_t p, std::int32_t q) { return p < q ? q : p; },
+      [=] CR_DEVICE(std::size_t i) { return x[i]; });
+}
+// pub fn fprefix(n, out: rw<f32>[n]@device, x: ro<f32>[n]@device) -> f32
+//   { let s = scan + parallel i in n yield x[i] into out; return s; }
+float ci_fprefix(std::size_t n, float* out, const float* x) {
+  return cr::gpu::scan_on<false, float>(
+      cr::gpu::here(), out, n, 0.0f, [] CR_DEVICE(float p, float q) { return static_cast<float>(p + q); },
+      [=] CR_DEVICE(std::size_t i) { return x[i]; });
+}
+// pub fn positives(n, out: rw<f32>[n]@device, x: ro<f32>[n]@device) -> usize
+//   { return compact parallel i in n where x[i] > 0.0 yield x[i] into out; }
+std::size_t ci_positives(std::size_t n, float* out, const float* x) {
+  return cr::gpu::compact_on(
+      cr::gpu::here(), out, n, [=] CR_DEVICE(std::size_t i) { return x[i] > 0.0f; },
+      [=] CR_DEVICE(std::size_t i) { return x[i]; });
+}
 }  // namespace
 
 extern "C" {
@@ -103,5 +140,41 @@ void cf_gemm(std::size_t m, std::size_t n, std::size_t k, std::size_t cn, float*
   cr::disjoint(c, cn, A, an);
   cr::disjoint(c, cn, B, bn);
   ci_gemm(m, n, k, c, cn, A, an, B, bn);
+}
+std::uint64_t cf_prefix(std::size_t n, std::uint64_t* out, const std::uint64_t* x) noexcept {
+  cr::view(out, n);
+  cr::view(x, n);
+  return ci_prefix(n, out, x);
+}
+std::uint32_t cf_wprefix(std::size_t n, std::uint32_t* out, const std::uint32_t* x) noexcept {
+  cr::view(out, n);
+  cr::view(x, n);
+  return ci_wprefix(n, out, x);
+}
+std::int32_t cf_runmax(std::size_t n, std::int32_t* out, const std::int32_t* x) noexcept {
+  cr::view(out, n);
+  cr::view(x, n);
+  return ci_runmax(n, out, x);
+}
+float cf_fprefix(std::size_t n, float* out, const float* x) noexcept {
+  cr::view(out, n);
+  cr::view(x, n);
+  return ci_fprefix(n, out, x);
+}
+std::size_t cf_positives(std::size_t n, float* out, const float* x) noexcept {
+  cr::view(out, n);
+  cr::view(x, n);
+  return ci_positives(n, out, x);
+}
+// Not a cairnc entry: the machine's inclusive u64 scan with a zero wait for predecessors, so that blocks which find
+// a predecessor unpublished take the look-back's escape (folding the inputs before their tile themselves).
+void cf_prefix_escape(std::size_t n, std::uint64_t* out, const std::uint64_t* x) noexcept {
+  std::size_t bytes = 0;
+  cr::gpu::b200::scan<false, std::uint64_t>(nullptr, bytes, x, out, n, cr::gpu::b200::Plus{}, nullptr);
+  void* temp = nullptr;
+  cr::gpu::check(cudaMalloc(&temp, bytes));
+  cr::gpu::b200::scan<false, std::uint64_t>(temp, bytes, x, out, n, cr::gpu::b200::Plus{}, nullptr, 0);
+  cr::gpu::check(cudaStreamSynchronize(nullptr));
+  cr::gpu::check(cudaFree(temp));
 }
 }

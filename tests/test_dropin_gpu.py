@@ -2,7 +2,10 @@
 (tests/dropin/emitted_program.cu): the reference's own cairn_exec.hpp and cairn_reuse.hpp, unchanged, run the B200
 machine, whose regions, collectors and multiply are this project's. Each cf_/cq_ entry is held to the oracle: saxpy
 and the u64 sum bit for bit, the f32 `reduce +` (the device path's f32 fold in an unspecified order,
-docs/numerics.md) within n * 2^-24 * sum |x|, the multiply within twice its contract bound.
+docs/numerics.md) within n * 2^-24 * sum |x|, the multiply within twice its contract bound. The scans and the
+compaction (cairn_reuse.hpp:430-524 over the machine's own single-pass scan, not CUB's): integer scans and the
+compaction bit for bit, the f32 scan within i * 2^-24 * sum |x[0..i]| at each i; sizes around the scan's tiles
+(4096 four-byte or 2048 eight-byte elements) and its 32-tile look-back window.
 
 The program is built by __graft_entry__.build() where the CAIRN reference tree is present; without the built
 library these tests are skipped, naming why."""
@@ -34,7 +37,10 @@ def emitted(cuda):
     for name, res, args in (("cf_saxpy", None, [z, p, p, p, C.c_float]), ("cf_saxpy4", None, [z, p, p, p, C.c_float]),
                             ("cq_saxpy", None, [p, z, p, p, p, C.c_float]), ("cf_dsum", C.c_float, [z, p]),
                             ("cf_usum", C.c_uint64, [z, p]), ("cf_vmax", C.c_int32, [z, p]),
-                            ("cf_gemm", None, [z, z, z, z, p, z, p, z, p])):
+                            ("cf_gemm", None, [z, z, z, z, p, z, p, z, p]), ("cf_prefix", C.c_uint64, [z, p, p]),
+                            ("cf_wprefix", C.c_uint32, [z, p, p]), ("cf_runmax", C.c_int32, [z, p, p]),
+                            ("cf_fprefix", C.c_float, [z, p, p]), ("cf_positives", C.c_size_t, [z, p, p]),
+                            ("cf_prefix_escape", None, [z, p, p])):
         f = getattr(h, name)
         f.restype, f.argtypes = res, args
     return h
@@ -87,3 +93,68 @@ def test_emitted_multiply_runs_the_tensor_cores(emitted, cuda, shape):
     bv = np.abs(inputs.decode("bf16", b).reshape(k, n))
     tol = 2 * (k + 1) * 2.0**-22 * (np.abs(c.reshape(m, n)) + av @ bv)
     assert (np.abs(ct.cpu().numpy().reshape(m, n) - want.reshape(m, n)) <= tol).all()
+
+
+SCAN_SIZES = [1, 31, 2048, 2049, 4096, 4097, 65 * 4096 + 7, 1_000_003]
+
+
+def _dev(a: np.ndarray, cuda) -> torch.Tensor:
+    return torch.from_numpy(a).to(cuda)
+
+
+@pytest.mark.parametrize("n", SCAN_SIZES)
+def test_emitted_integer_scans(emitted, cuda, n):
+    rng = np.random.default_rng(n)
+    x = rng.integers(0, 1 << 40, n, dtype=np.uint64)
+    xt, out = _dev(x.view(np.int64), cuda), torch.empty(n, dtype=torch.int64, device=cuda)
+    total = emitted.cf_prefix(n, out.data_ptr(), xt.data_ptr())
+    want = np.cumsum(x, dtype=np.uint64)
+    assert np.array_equal(out.cpu().numpy().view(np.uint64), want) and total == int(want[-1])
+
+    w = rng.integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
+    wt, wout = _dev(w.view(np.int32), cuda), torch.empty(n, dtype=torch.int32, device=cuda)
+    wtotal = emitted.cf_wprefix(n, wout.data_ptr(), wt.data_ptr())
+    wwant = np.cumsum(w, dtype=np.uint32)  # add_wrap: modulo 2^32
+    assert np.array_equal(wout.cpu().numpy().view(np.uint32), wwant) and wtotal == int(wwant[-1])
+
+    v = rng.integers(-2**31, 2**31 - 1, n, dtype=np.int64).astype(np.int32)
+    vt, vout = _dev(v, cuda), torch.empty(n, dtype=torch.int32, device=cuda)
+    vtotal = emitted.cf_runmax(n, vout.data_ptr(), vt.data_ptr())
+    run = np.maximum.accumulate(v)
+    want_ex = np.concatenate([[np.int32(-2**31)], run[:-1]]).astype(np.int32)
+    assert np.array_equal(vout.cpu().numpy(), want_ex) and vtotal == int(run[-1])
+
+
+@pytest.mark.parametrize("n", [1, 4097, 1_000_003])
+def test_emitted_f32_scan(emitted, cuda, n):
+    x = np.random.default_rng(n + 1).uniform(-1, 1, n).astype(np.float32)
+    out = torch.empty(n, dtype=torch.float32, device=cuda)
+    total = emitted.cf_fprefix(n, out.data_ptr(), _dev(x, cuda).data_ptr())
+    got = out.cpu().numpy().astype(np.float64)
+    exact = np.cumsum(x.astype(np.float64))
+    idx = np.arange(1, n + 1)
+    tol = idx * 2.0**-24 * np.cumsum(np.abs(x).astype(np.float64)) + 1e-30
+    assert (np.abs(got - exact) <= tol).all()
+    assert total == np.float32(got[-1])
+
+
+@pytest.mark.parametrize("n", [1, 2, 4097, 1_000_003])
+def test_emitted_compaction_keeps_order(emitted, cuda, n):
+    x = np.random.default_rng(n + 2).standard_normal(n).astype(np.float32)
+    out = torch.full((n,), -7.0, dtype=torch.float32, device=cuda)
+    used = emitted.cf_positives(n, out.data_ptr(), _dev(x, cuda).data_ptr())
+    keep = x[x > 0]
+    got = out.cpu().numpy()
+    assert used == keep.size
+    assert np.array_equal(got[:used].view(np.uint32), keep.view(np.uint32))
+    assert (got[used:] == -7.0).all()  # the tail of out is left alone
+
+
+@pytest.mark.parametrize("n", [5000, 200_003])
+def test_scan_look_back_escape_gives_the_same_prefixes(emitted, cuda, n):
+    """With no time to wait, every block that finds a predecessor unpublished folds the inputs before its tile
+    itself: the answer is the same."""
+    x = np.random.default_rng(n + 3).integers(0, 1 << 40, n, dtype=np.uint64)
+    out = torch.empty(n, dtype=torch.int64, device=cuda)
+    emitted.cf_prefix_escape(n, out.data_ptr(), _dev(x.view(np.int64), cuda).data_ptr())
+    assert np.array_equal(out.cpu().numpy().view(np.uint64), np.cumsum(x, dtype=np.uint64))
