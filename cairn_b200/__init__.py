@@ -6,7 +6,7 @@ torch-facing forms of its entries (cairn_b200.ops) and the range-sharded multi-G
 """
 
 from ._lib import CairnError, LIB_PATH, header_symbols, lib
-from .ops import gemm, mma_unordered, reduce_sum, saxpy, stream_status
+from .ops import gemm, mma_unordered, reduce_sum, saxpy, stream_status, watchdog_selftest
 
 __all__ = [
     "CairnError",
@@ -18,5 +18,6 @@ __all__ = [
     "reduce_sum",
     "saxpy",
     "stream_status",
+    "watchdog_selftest",
 ]
 __version__ = "0.1.0"

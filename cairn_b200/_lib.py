@@ -48,6 +48,7 @@ SIGNATURES: dict[str, tuple] = {
     "cairn_b200_sum_u64": (_i, [_p, _z, _p, _p, _p]),
     "cairn_b200_sum_u64_host": (_i, [_p, _z, _p, C.POINTER(C.c_uint64), _ip]),
     "cairn_b200_stream_status": (_i, [_p]),
+    "cairn_b200_watchdog_selftest": (_i, [_p]),
     "cairn_b200_status_string": (C.c_char_p, [_i]),
     "cairn_b200_sm_count": (_i, []),
     "cairn_b200_version": (_i, []),

@@ -460,6 +460,17 @@ int cairn_b200_sum_f32_combine_device(void* stream, const double* parts, size_t 
   return cuda_status(combine_f32_parts_launch(parts, static_cast<int>(count), out, static_cast<cudaStream_t>(stream)));
 }
 
+int cairn_b200_watchdog_selftest(void* stream) {
+  int status;
+  const Device* d = current(&status);
+  if (!d) return status;
+  if ((status = cairn_b200_stream_status(stream)) != CAIRN_B200_OK) return status;  // start from a clear fault word
+  if (watchdog_launch(static_cast<cudaStream_t>(stream), d->fault) != cudaSuccess) return CAIRN_B200_ERR_CUDA;
+  status = cairn_b200_stream_status(stream);
+  if (status == CAIRN_B200_ERR_TIMEOUT) return CAIRN_B200_OK;  // the wait gave up, and its fault came back
+  return status == CAIRN_B200_OK ? CAIRN_B200_ERR_DEVICE : status;
+}
+
 int cairn_b200_stream_status(void* stream) {
   const cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return CAIRN_B200_ERR_CUDA;

@@ -16,6 +16,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include "gemm.h"
+#include "ptx.cuh"
 
 namespace cb {
 
@@ -465,6 +466,25 @@ cudaError_t sum_u64_launch(std::size_t n, const std::uint64_t* x, std::uint64_t*
   auto* oo = reinterpret_cast<unsigned long long*>(out);
   if (aligned16(x)) sum_u64_kernel<true><<<grid, T, 0, s>>>(n, xx, oo, overflow, partials, ticket);
   else sum_u64_kernel<false><<<grid, T, 0, s>>>(n, xx, oo, overflow, partials, ticket);
+  return cudaGetLastError();
+}
+
+// The watchdog self-test: one thread waits, through the same bounded mbarrier wait every kernel here uses, on a
+// barrier that nothing arrives at. The wait gives up after WAIT_LIMIT_NS, records FAULT_WATCHDOG and returns.
+__global__ void watchdog_kernel(std::uint32_t* fault) {
+  __shared__ __align__(8) std::uint64_t never;
+  __shared__ std::uint32_t abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&never, 1);
+    abort_flag = 0u;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(&never, 0u, &abort_flag, fault, FAULT_WATCHDOG);
+}
+
+cudaError_t watchdog_launch(cudaStream_t s, std::uint32_t* fault) {
+  watchdog_kernel<<<1, 32, 0, s>>>(fault);
   return cudaGetLastError();
 }
 

@@ -163,3 +163,10 @@ def stream_status(device: torch.device | int | None = None) -> None:
     bound) was recorded."""
     stream = torch.cuda.current_stream(device).cuda_stream
     check(lib().cairn_b200_stream_status(stream), "stream_status")
+
+
+def watchdog_selftest(device: torch.device | int | None = None) -> None:
+    """Runs the device watchdog's self-test on the current stream (a bounded wait on a barrier nothing completes
+    must give up and report its fault); raises CairnError if it did not."""
+    stream = torch.cuda.current_stream(device).cuda_stream
+    check(lib().cairn_b200_watchdog_selftest(stream), "watchdog_selftest")

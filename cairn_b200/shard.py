@@ -12,16 +12,23 @@ operations allow:
   sharded_sum_u64            each rank's (wrapped total, overflow flag) is all-gathered and folded in rank order
                              with cr::Sum's rule (runtime/cairn_runtime.hpp:158-166): the flag is set exactly when
                              the whole sum does not fit.
+
+Failure detection (the reference has none across devices; its device guards trap): a rank that leaves between steps
+is found on the host. `Liveness` marks each rank's arrival at a step in the process group's store, and `require`
+raises CairnError(ERR_TIMEOUT) naming the ranks that did not arrive within a deadline, before any collective or
+kernel of the step is queued. A collective that a peer never joins ends with the process group's own timeout; the
+sums' exchanges turn that error into the same CairnError, so no rank waits on a lost peer for ever.
 """
 
 from __future__ import annotations
 
 import ctypes as C
+from datetime import timedelta
 
 import torch
 import torch.distributed as dist
 
-from ._lib import ERR_OVERFLOW, CairnError, check, lib
+from ._lib import ERR_OVERFLOW, ERR_TIMEOUT, CairnError, check, lib
 from .ops import gemm, reduce_sum, saxpy
 
 
@@ -42,6 +49,43 @@ def sharded_gemm(a_block: torch.Tensor, b: torch.Tensor, **kw) -> torch.Tensor:
 
 def sharded_saxpy(a: float, x_local: torch.Tensor, y_local: torch.Tensor, out_local: torch.Tensor | None = None):
     return saxpy(a, x_local, y_local, out_local)
+
+
+class Liveness:
+    """Which ranks reached a step, kept in a torch.distributed store shared by the ranks (the process group's own,
+    a TCPStore or a FileStore). Each rank marks a step as it begins it; `missing` lists the other ranks that have not
+    marked it within a deadline, and `require` raises CairnError(ERR_TIMEOUT) naming them."""
+
+    def __init__(self, store, rank: int, world: int, prefix: str = "cairn_b200/alive"):
+        self.store, self.rank, self.world, self.prefix = store, rank, world, prefix
+
+    def _key(self, step: int, rank: int) -> str:
+        return f"{self.prefix}/{step}/{rank}"
+
+    def mark(self, step: int) -> None:
+        self.store.set(self._key(step, self.rank), "1")
+
+    def missing(self, step: int, timeout_s: float) -> list[int]:
+        others = [r for r in range(self.world) if r != self.rank]
+        try:
+            self.store.wait([self._key(step, r) for r in others], timedelta(seconds=timeout_s))
+            return []
+        except Exception:  # the store's timeout: find which ranks it was waiting for
+            return [r for r in others if not self.store.check([self._key(step, r)])]
+
+    def require(self, step: int, timeout_s: float) -> None:
+        gone = self.missing(step, timeout_s)
+        if gone:
+            raise CairnError(ERR_TIMEOUT, f"step {step}: ranks {gone} did not arrive within {timeout_s} s")
+
+
+def _all_gather(out: torch.Tensor, part: torch.Tensor, group, what: str) -> None:
+    """dist.all_gather_into_tensor, with a lost peer (the process group's timeout, or a closed connection) reported
+    as CairnError(ERR_TIMEOUT)."""
+    try:
+        dist.all_gather_into_tensor(out, part, group=group)
+    except (RuntimeError, dist.DistError) as e:
+        raise CairnError(ERR_TIMEOUT, f"{what}: a rank did not join the exchange ({type(e).__name__})") from e
 
 
 def combine_f32_parts(parts: torch.Tensor) -> float:
@@ -69,7 +113,7 @@ def sharded_sum_f32(x_local: torch.Tensor, group=None) -> float:
     part = torch.empty(3, dtype=torch.float64, device=x_local.device)
     reduce_sum(x_local, out=part)
     flat = torch.empty(world * 3, dtype=torch.float64, device=x_local.device)
-    dist.all_gather_into_tensor(flat, part, group=group)
+    _all_gather(flat, part, group, "sharded_sum_f32")
     parts = flat.view(world, 3)
     if parts.is_cuda:
         total = torch.empty(1, dtype=torch.float32, device=parts.device)
@@ -87,8 +131,8 @@ def sharded_sum_u64(x_local: torch.Tensor, group=None) -> int:
     reduce_sum(x_local, out=cell.view(torch.uint64), overflow=flag)
     cells = torch.zeros(world, dtype=torch.int64, device=x_local.device)
     flags = torch.zeros(world, dtype=torch.int32, device=x_local.device)
-    dist.all_gather_into_tensor(cells, cell, group=group)
-    dist.all_gather_into_tensor(flags, flag, group=group)
+    _all_gather(cells, cell, group, "sharded_sum_u64")
+    _all_gather(flags, flag, group, "sharded_sum_u64")
     total, over = fold_u64([int(v) & (2**64 - 1) for v in cells.cpu().tolist()], flags.cpu().tolist())
     if over:
         raise CairnError(ERR_OVERFLOW, "sharded_sum_u64")

@@ -146,6 +146,12 @@ int cairn_b200_sum_f32_noalloc(void* stream, size_t n, const float* x, float* ou
  * (runtime/cairn_reuse.hpp:125-141 give_back waits on the lane's stream). */
 int cairn_b200_stream_status(void* stream);
 const char* cairn_b200_status_string(int status);
+/* The device watchdog's self-test, synchronous on `stream`: one block waits, through the bounded wait every kernel
+ * of this library uses, on a shared-memory barrier that nothing completes; the wait gives up after its 2 s limit
+ * and records a fault, which this call reads back and clears. Returns CAIRN_B200_OK when all of that happened (the
+ * context stays usable), CAIRN_B200_ERR_DEVICE when no fault came back, or the failing status. No reference
+ * counterpart: the reference's device guards trap and poison the context (runtime/cairn_kernels.hpp:33-59). */
+int cairn_b200_watchdog_selftest(void* stream);
 /* The number of SMs of the current device the kernels size their grids for, or a negative status. */
 int cairn_b200_sm_count(void);
 /* The ABI version: major * 10000 + minor * 100 + patch. */
