@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of CAIRN's data-parallel hot path on B200, one JSON line per run (rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm|gemm5|mlp|saxpy|sum_f32|sum_u64]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--workload gemm|gemm5|mlp|saxpy|sum_f32|sum_u64|scan]
                     [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...        (one rank per GPU, NCCL)
 
@@ -17,6 +17,10 @@ Workloads (the default is the one the headline metric is 
   sum_f32  config 4: `reduce +` over n = 2^30 f32 (exact sum rounded once), range-sharded; the ranks' parts meet in
            one NCCL all-gather and a combine kernel on every rank.
   sum_u64  config 4: checked `reduce +` over n = 2^30 u64 (data[i] = i), range-sharded, parts all-gathered.
+  scan     the next row after reduce: `scan add_wrap parallel i in n yield x[i] into out` over n = 2^30 u32 through
+           a CAIRN program built over the drop-in runtime headers (tests/dropin: the reference's own context code on
+           this project's B200 machine and scan kernel); one replica per rank: weak scaling. The roofline times the
+           machine's scan kernel alone.
 Inputs are synthetic (seeded torch generators on the device), larger than L2 across the timed steps: every step
 reads a different buffer set, or (2^30 workloads) buffers far larger than the 126 MB L2.
 
@@ -246,13 +250,19 @@ def cpu_stream_sample(workload: str, budget_s: float):
     x = rng.uniform(-1, 1, n).astype(np.float32)
     y = rng.uniform(-1, 1, n).astype(np.float32)
     u = np.arange(n, dtype=np.uint64)
+    w = x.view(np.uint32)
     out = np.empty_like(x)
     lib = reference if kind == "reference" else restated
-    per = {"saxpy": 12, "sum_f32": 4, "sum_u64": 8}[workload]
+    per = {"saxpy": 12, "sum_f32": 4, "sum_u64": 8, "scan": 8}[workload]
     spent, done = 0.0, 0
     while spent < budget_s:
         t = time.perf_counter()
-        if workload == "saxpy":
+        if workload == "scan":
+            if kind == "reference":
+                reference.scan_u32(w, out.view(np.uint32))
+            else:
+                restated.scan_u32(w)
+        elif workload == "saxpy":
             if kind == "reference":
                 reference.saxpy(2.5, x, y, out)
             else:
@@ -430,6 +440,58 @@ class Stream:
         return self.dist.world * chunk * self.bytes / (ms * 1e-3) / 1e9, h2d, d2h
 
 
+EMITTED = ROOT / "tests" / "dropin" / "_build" / "libemitted.so"
+
+
+class Scan:
+    """The drop-in machine's device scan over n = 2^30 u32 (add_wrap), through an emitted-style CAIRN library built
+    over include/cairn_b200/runtime (cq_wscan: the reference's scan_into, which scans into its arena and copies to
+    out), and the machine's scan kernel alone (b200_scan_u32) for the roofline. 8 algorithmic bytes per element."""
+
+    def __init__(self, dist: Dist, log2n: int = 30):
+        import torch
+
+        self.torch, self.dist = torch, dist
+        self.n = 1 << log2n
+        dev = dist.device
+        g = torch.Generator(device=dev).manual_seed(0 + dist.rank)
+        self.x = torch.randint(-2**31, 2**31 - 1, (self.n,), device=dev, dtype=torch.int32, generator=g)
+        self.out = torch.empty_like(self.x)
+        lib_handle()  # the program links libcairn_b200.so: load it from the tree first
+        h = C.CDLL(str(EMITTED))
+        h.cq_wscan.restype, h.cq_wscan.argtypes = None, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]
+        h.b200_scan_u32_scratch.restype, h.b200_scan_u32_scratch.argtypes = C.c_size_t, [C.c_size_t]
+        h.b200_scan_u32.restype = None
+        h.b200_scan_u32.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p]
+        self.h = h
+        self.temp = torch.empty(h.b200_scan_u32_scratch(self.n), dtype=torch.uint8, device=dev)
+        self.stream = torch.cuda.current_stream(dev)
+        self.bytes = 8
+        self.scaling = "weak"
+
+    def launch(self, i: int):
+        self.h.cq_wscan(self.stream.cuda_stream, self.n, self.out.data_ptr(), self.x.data_ptr())
+
+    def kernel_alone(self, i: int):
+        self.h.b200_scan_u32(self.stream.cuda_stream, self.n, self.out.data_ptr(), self.x.data_ptr(),
+                             self.temp.data_ptr())
+
+    def e2e(self, steps: int, warmup: int):
+        torch = self.torch
+        chunk = min(self.n, 1 << 26)  # the e2e sample: 2^26 elements from pinned host memory
+        x_h = self.x[:chunk].cpu().pin_memory()
+        o_h = torch.empty(chunk, dtype=torch.int32).pin_memory()
+        x_d, o_d, st = self.x[:chunk], self.out[:chunk], self.stream.cuda_stream
+
+        def step(i):
+            x_d.copy_(x_h, non_blocking=True)
+            self.h.cq_wscan(st, chunk, o_d.data_ptr(), x_d.data_ptr())
+            o_h.copy_(o_d, non_blocking=True)
+
+        ms, _, _, _ = time_steps(self.dist, self.stream, step, steps, warmup, per_launch=False)
+        return self.dist.world * chunk * self.bytes / (ms * 1e-3) / 1e9, 4 * chunk, 4 * chunk
+
+
 class Mlp:
     """Config 3: one forward + backward of a 2-layer MLP (batch 8192, 4096 -> 16384 -> 4096, bf16 weights ~ N(0, 0.02),
     inputs ~ N(0, 1), ReLU, MSE against an N(0, 1) target): six products and the fused loss kernel per step.
@@ -531,6 +593,8 @@ def reference_arm(args, dist: Dist) -> None:
             "cpu_baseline": {"value": value, "unit": unit, "cores": cores, "kind": kind,
                              "sample": f"per step: {sample}"},
             "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    if args.workload == "scan":
+        line["scaling"], line["dtype"] = "weak", "u32"
     if not reference.available():
         line["note"] = "oracle/_ref not built on this box: the C restatement of the reference's host path ran"
     print(json.dumps(line), flush=True)
@@ -549,6 +613,9 @@ def config_of(args, dist: Dist) -> dict:
     if w == "gemm5":
         return {"workload": "config 5: M-sharded bf16 GEMM, f32 out", "m": 65536, "n": 8192, "k": 8192,
                 "parallelism": f"row-block x{dist.world}", "l2": "inputs rotate over buffer sets larger than L2"}
+    if w == "scan":
+        return {"workload": f"drop-in scan: add_wrap over n = 2^{args.log2n} u32 (next row after reduce)",
+                "n": 1 << args.log2n, "parallelism": f"replicas x{dist.world}", "l2": "inputs larger than L2"}
     return {"workload": f"config 4: {w} over n = 2^{args.log2n}", "n": 1 << args.log2n,
             "parallelism": f"range x{dist.world}", "l2": "inputs larger than L2"}
 
@@ -558,13 +625,14 @@ def main() -> None:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=None)
-    ap.add_argument("--workload", default="gemm", choices=["gemm", "gemm5", "mlp", "saxpy", "sum_f32", "sum_u64"])
+    ap.add_argument("--workload", default="gemm",
+                    choices=["gemm", "gemm5", "mlp", "saxpy", "sum_f32", "sum_u64", "scan"])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--log2n", type=int, default=30, help="saxpy/sum size 2^log2n (BASELINE: 30; smaller for ncu)")
     args = ap.parse_args()
     defaults = {"gemm": (2000, 50), "gemm5": (50, 5), "mlp": (40, 5), "saxpy": (100, 5), "sum_f32": (200, 5),
-                "sum_u64": (100, 5)}
+                "sum_u64": (100, 5), "scan": (50, 5)}
     d_steps, d_warm = defaults[args.workload] if args.impl == "ours" else (5, 1)
     args.steps = args.steps if args.steps is not None else d_steps
     args.warmup = args.warmup if args.warmup is not None else d_warm
@@ -582,6 +650,15 @@ def main() -> None:
         wl = Gemm(dist, args.workload == "gemm5")
     elif args.workload == "mlp":
         wl = Mlp(dist)
+    elif args.workload == "scan":
+        if not EMITTED.exists():
+            if dist.rank == 0:
+                print(json.dumps({"metric": BASELINE_METRIC, "workload": "scan", "unavailable":
+                                  "tests/dropin/_build/libemitted.so is not built (it needs the CAIRN reference's "
+                                  "runtime headers, present where __graft_entry__.build() ran)"}), flush=True)
+            dist.close()
+            return
+        wl = Scan(dist, args.log2n)
     else:
         wl = Stream(dist, args.workload, args.log2n)
     peaks, peak_source = measured_peaks()
@@ -589,6 +666,8 @@ def main() -> None:
     ms, launch_ms, t0, t1 = time_steps(dist, wl.stream, wl.launch, args.steps, args.warmup)
     clocks = sampler.window(t0, t1)
     sampler.stop()
+    if isinstance(wl, Scan):  # the roofline's kernel: the machine's scan alone, without the context's copy pass
+        _, launch_ms, _, _ = time_steps(dist, wl.stream, wl.kernel_alone, args.steps, args.warmup)
     stat = lib_handle().cairn_b200_stream_status(wl.stream.cuda_stream)
     if stat:
         raise SystemExit(f"device status {stat} after the timed steps")
@@ -602,16 +681,17 @@ def main() -> None:
         long_step = isinstance(wl, Mlp) or args.workload == "gemm5"
         peak = peaks.get("bf16_tflops_sustained" if long_step else "bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
         kernel = "tc_gemm_pair_kernel"
-        traffic = profile_traffic({"gemm": "gemm_bf16_4096_bias_relu", "gemm5": "gemm_bf16_config5",
+        traffic = profile_traffic({"gemm": "gemm_pair_bf16_4096_bias_relu", "gemm5": "gemm_bf16_config5",
                                    "mlp": "mlp_step_config3"}[args.workload])
     else:
         per_rank_bytes = wl.n * wl.bytes
         value = dist.world * per_rank_bytes / (ms * 1e-3) / 1e9
         unit, bound = "GB/s", "hbm"
-        dtype = {"saxpy": "f32", "sum_f32": "f32", "sum_u64": "u64"}[args.workload]
+        dtype = {"saxpy": "f32", "sum_f32": "f32", "sum_u64": "u64", "scan": "u32"}[args.workload]
         achieved = per_rank_bytes / (launch_ms * 1e-3) / 1e9
         peak = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
-        kernel = {"saxpy": "saxpy_vec_kernel", "sum_f32": "sum_f32_kernel", "sum_u64": "sum_u64_kernel"}[args.workload]
+        kernel = {"saxpy": "saxpy_vec_kernel", "sum_f32": "sum_f32_kernel", "sum_u64": "sum_u64_kernel",
+                  "scan": "scan_kernel"}[args.workload]
         traffic = profile_traffic(f"{args.workload}_2p30")
 
     cpu = None
@@ -624,12 +704,13 @@ def main() -> None:
             v, cores, kind, sample = cpu_stream_sample(args.workload, 12.0)
         cpu = {"value": v, "unit": unit, "cores": cores, "kind": kind, "sample": sample}
 
-    launches = args.steps * (7 if isinstance(wl, Mlp) else
+    launches = args.steps * (7 if isinstance(wl, Mlp) else 2 if isinstance(wl, Scan) else
                              1 if isinstance(wl, Gemm) or args.workload != "sum_f32" or dist.world == 1 else 2)
     line = {
         "metric": BASELINE_METRIC, "value": value, "unit": unit, "n_gpus": dist.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": wl.scaling if isinstance(wl, (Gemm, Mlp)) else "strong", "vs_baseline": None, "dtype": dtype,
+        "scaling": wl.scaling if isinstance(wl, (Gemm, Mlp, Scan)) else "strong", "vs_baseline": None,
+        "dtype": dtype,
         "data": "synthetic (seeded device generators; random-init operands of the configs' shapes and distributions)",
         "config": config_of(args, dist),
         "roofline": {"bound": bound, "kernel": kernel, "achieved": achieved, "peak": peak, "unit": unit,

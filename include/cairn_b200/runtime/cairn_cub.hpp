@@ -11,8 +11,8 @@
 //
 // B200::inclusive_scan and exclusive_sum: one pass over the input with decoupled look-back (Merrill and Garland,
 // "Single-pass Parallel Prefix Scan with Decoupled Look-back", NVIDIA technical report NVR-2016-002). Each block
-// takes the next tile in launch order from an atomic counter, scans it in registers (eight warps, each a contiguous
-// run of 32-element rows: a shuffle scan per row, carried row to row), publishes the tile's aggregate, then looks
+// takes the next tile in launch order from an atomic counter, scans it in shared memory (coalesced rows in, each
+// thread's contiguous segment in sequence, the segments' totals across the block), publishes its aggregate, looks
 // back over its predecessors' published aggregates and inclusive prefixes, 32 tiles per step, until it meets an
 // inclusive prefix, and publishes its own. The operator must be associative (commutativity is not assumed: every
 // fold keeps the elements' order). Every wait for a predecessor is bounded; a block that waited longer than the
@@ -101,13 +101,32 @@ __global__ void __launch_bounds__(FOLD_THREADS)
 
 // ---- scan ------------------------------------------------------------------------------------------------------
 
-constexpr unsigned SCAN_THREADS = 256;
+// A block scans a 64 KB tile held in shared memory (three blocks resident per SM). Eight worker warps load the tile
+// in coalesced 32-element rows, then each thread scans its own contiguous segment of S elements in sequence
+// (raking), the 256 segment totals are scanned across the block, and the workers write the rows out with their
+// prefixes. A ninth warp starts the look-back over the predecessors as the tile starts, so it runs while the
+// workers load and rake rather than after them.
+constexpr unsigned SCAN_THREADS = 256;                   // the tile's workers: load, rake, write
 constexpr unsigned SCAN_WARPS = SCAN_THREADS / 32;
+constexpr unsigned SCAN_BLOCK = SCAN_THREADS + 32;       // and one more warp that looks back meanwhile
+constexpr unsigned SCAN_BLOCKS_PER_SM = 3;
+constexpr unsigned SCAN_LOAD_BATCH = 16;  // rows a warp loads per batch (two batches in flight)
 constexpr std::uint64_t SCAN_WAIT_NS = 2000000000ull;  // how long a block waits for its predecessors
 
-// Rows of 32 elements each warp scans: 64 bytes of values per lane.
-template<class T> constexpr unsigned scan_rows() noexcept { return sizeof(T) <= 4 ? 16u : sizeof(T) <= 8 ? 8u : 4u; }
-template<class T> constexpr std::size_t scan_tile() noexcept { return std::size_t(SCAN_THREADS) * scan_rows<T>(); }
+// Elements per thread's segment (and rows per warp): 64 KB of values per tile where the value allows, 16, 32 or 64
+// (whole batches of SCAN_LOAD_BATCH rows).
+template<class T> constexpr unsigned scan_segment() noexcept {
+  constexpr std::size_t s = (64 * 1024) / (std::size_t(SCAN_THREADS) * sizeof(T));
+  return s >= 64 ? 64u : s >= 32 ? 32u : 16u;
+}
+template<class T> constexpr std::size_t scan_tile() noexcept { return std::size_t(SCAN_THREADS) * scan_segment<T>(); }
+// Shared memory holds element e at e + e / S: one pad per segment, so rows (32 consecutive elements) and segments
+// (S consecutive elements, one per thread) are both read and written without bank conflicts.
+template<class T> constexpr std::size_t scan_smem() noexcept {
+  return (scan_tile<T>() + SCAN_THREADS) * sizeof(T) + SCAN_THREADS * sizeof(T) + SCAN_THREADS;
+}
+// The worker warps' own barrier (the look-back warp does not take part).
+__device__ inline void workers_sync() { asm volatile("bar.sync 1, %0;" ::"n"(SCAN_THREADS) : "memory"); }
 constexpr std::size_t round256(std::size_t b) noexcept { return (b + 255) / 256 * 256; }
 
 // A value that may be absent (no identity is known to an inclusive scan).
@@ -129,6 +148,19 @@ __device__ inline unsigned load_acquire(const unsigned* p) {
 __device__ inline void store_release(unsigned* p, unsigned v) {
   asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+__device__ inline unsigned long long load_acquire(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ inline unsigned long long load_relaxed(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ inline void store_relaxed(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 
 // A warp shuffle of any trivially copyable value, a 32-bit word at a time; `move` shuffles one word.
 template<class T, class Move> __device__ inline T shuffled(const T& v, Move move) {
@@ -144,6 +176,41 @@ template<class T, class Move> __device__ inline T shuffled(const T& v, Move move
 
 // Tile states: 0 nothing yet, 1 its aggregate is published, 2 its inclusive prefix is published.
 constexpr unsigned TILE_AGGREGATE = 1, TILE_PREFIX = 2;
+
+// The tiles' published states and values. A value of four bytes or fewer shares one 64-bit word with its state (the
+// state in the high half): one relaxed load gets both, and nothing else is read on the strength of it, so no fence
+// is needed. A larger value sits in its own array (aggregate or inclusive prefix), written before the state word is
+// released and read after it is acquired.
+template<class T> struct TileStates {
+  static constexpr bool PACKED = sizeof(T) <= 4;
+  unsigned long long* words;  // PACKED
+  unsigned* flags;            // otherwise
+  T* aggregate;
+  T* inclusive;
+  __device__ void publish(std::size_t t, unsigned state, const T& v) const {
+    if constexpr(PACKED) {
+      unsigned bits = 0;
+      std::memcpy(&bits, &v, sizeof(T));
+      store_relaxed(words + t, (static_cast<unsigned long long>(state) << 32) | bits);
+    } else {
+      (state == TILE_PREFIX ? inclusive : aggregate)[t] = v;
+      store_release(flags + t, state);
+    }
+  }
+  // Tile t's state (0: not yet published) and, once published, its value.
+  __device__ unsigned read(std::size_t t, T& v) const {
+    if constexpr(PACKED) {
+      const unsigned long long w = load_relaxed(words + t);
+      const unsigned bits = static_cast<unsigned>(w);
+      std::memcpy(&v, &bits, sizeof(T));
+      return static_cast<unsigned>(w >> 32);
+    } else {
+      const unsigned f = load_acquire(flags + t);
+      if(f) v = read_fresh(f == TILE_PREFIX ? inclusive + t : aggregate + t);
+      return f;
+    }
+  }
+};
 
 // Lane 0's result: op over [begin, end) of the inputs, in order (the look-back's escape when a predecessor is late).
 template<class T, class In, class Fold>
@@ -164,140 +231,229 @@ __device__ inline Part<T> fold_range_warp(In in, std::size_t begin, std::size_t 
   return acc;
 }
 
+// Predecessors each lane of the looking-back warp reads per step (lane l reads the l-th nearest: one coalesced
+// 256-byte read a step). Measured on a B200 at n = 2^30: 4 or 8 per lane read more lines per step at the frontier
+// every look-back warp is reading, and ran slower.
+constexpr unsigned LOOK_PER_LANE = 1;
+
 // Warp 0's look-back for tile t > 0: op over every element before the tile, in lane 0.
 template<class T, class In, class Fold>
-__device__ inline Part<T> look_back(In in, std::size_t t, std::size_t tile_elems, Fold& fold, const unsigned* flags,
-                                    const T* aggregate, const T* inclusive, std::uint64_t wait_ns, unsigned lane) {
+__device__ inline Part<T> look_back(In in, std::size_t t, std::size_t tile_elems, Fold& fold, const TileStates<T>& st,
+                                    std::uint64_t wait_ns, unsigned lane) {
+  constexpr int K = LOOK_PER_LANE;
   Part<T> run{T{}, false};
   long long end = static_cast<long long>(t) - 1;
   const std::uint64_t start = globaltimer();
   for(;;) {
-    const long long pred = end - static_cast<long long>(lane);
-    unsigned f = TILE_PREFIX;  // before tile 0 nothing is missing
-    if(pred >= 0) {
-      while((f = load_acquire(flags + pred)) == 0)
-        if(globaltimer() - start > wait_ns) break;
+    // lane l reads tiles end - K l - k for k = 0 (the newest) .. K - 1; before tile 0 nothing is missing
+    T v[K];
+    unsigned f[K];
+#pragma unroll
+    for(int k = 0; k < K; ++k) {
+      const long long pred = end - K * static_cast<long long>(lane) - k;
+      v[k] = T{};
+      f[k] = pred >= 0 ? st.read(static_cast<std::size_t>(pred), v[k]) : TILE_PREFIX;
     }
-    if(__any_sync(~0u, f == 0)) return fold_range_warp<T>(in, 0, t * tile_elems, fold, lane);
-    T v = T{};
-    if(pred >= 0) v = read_fresh(f == TILE_PREFIX ? inclusive + pred : aggregate + pred);
-    const unsigned prefixes = __ballot_sync(~0u, f == TILE_PREFIX);
-    const unsigned stop = prefixes ? __ffs(prefixes) - 1 : 31;  // the nearest predecessor holding a prefix
-    bool ok = pred >= 0 && lane <= stop;
+    bool missing = false;
+#pragma unroll
+    for(int k = 0; k < K; ++k) {
+      const long long pred = end - K * static_cast<long long>(lane) - k;
+      unsigned pause = 32;  // ns; doubled up to 128 so waiting lanes neither crowd the lines being published nor
+                            // sleep long past the moment a predecessor publishes (the workers wait on this warp)
+      while(pred >= 0 && f[k] == 0) {
+        if(globaltimer() - start > wait_ns) break;
+        __nanosleep(pause);
+        pause = pause < 128 ? 2 * pause : pause;
+        f[k] = st.read(static_cast<std::size_t>(pred), v[k]);
+      }
+      missing = missing || f[k] == 0;
+    }
+    if(__any_sync(~0u, missing)) return fold_range_warp<T>(in, 0, t * tile_elems, fold, lane);
+    int nearest = K;  // this lane's nearest predecessor holding a prefix (or standing before tile 0)
+#pragma unroll
+    for(int k = K - 1; k >= 0; --k)
+      if(f[k] == TILE_PREFIX) nearest = k;
+    const unsigned holders = __ballot_sync(~0u, nearest < K);
+    const unsigned stop = holders ? __ffs(holders) - 1 : 31;  // the nearest lane holding one
+    // this lane's share, oldest first: every tile newer than the nearest prefix in the window, and that prefix
+    Part<T> mine{T{}, false};
+    if(lane <= stop) {
+      const int top = lane == stop ? nearest : K - 1;
+#pragma unroll
+      for(int k = K - 1; k >= 0; --k) {
+        const long long pred = end - K * static_cast<long long>(lane) - k;
+        if(k > top || pred < 0) continue;
+        mine = mine.ok ? Part<T>{fold(mine.v, v[k]), true} : Part<T>{v[k], true};
+      }
+    }
+    T w = mine.v;
+    bool ok = mine.ok;
 #pragma unroll
     for(unsigned d = 1; d < 32; d <<= 1) {  // lane + d holds earlier tiles
-      const T o = shuffled(v, [&](unsigned w) { return __shfl_down_sync(~0u, w, d); });
+      const T o = shuffled(w, [&](unsigned x) { return __shfl_down_sync(~0u, x, d); });
       const bool ook = __shfl_down_sync(~0u, ok ? 1 : 0, d) && lane + d < 32;
       if(ook) {
-        v = ok ? fold(o, v) : o;
+        w = ok ? fold(o, w) : o;
         ok = true;
       }
     }
-    if(ok) run = run.ok ? Part<T>{fold(v, run.v), true} : Part<T>{v, true};  // meaningful in lane 0
-    if(prefixes) return run;
-    end -= 32;
+    if(ok) run = run.ok ? Part<T>{fold(w, run.v), true} : Part<T>{w, true};  // meaningful in lane 0
+    if(holders) return run;
+    end -= 32 * K;
   }
 }
 
 // One tile per block. Inclusive: out[i] = op over in[0..i]. Exclusive: out[0] = T{} and out[i] = op over in[0..i)
 // (used for the exclusive sum, whose T{} is zero).
 template<bool Exclusive, class T, class In, class Out, class Fold>
-__global__ void __launch_bounds__(SCAN_THREADS)
-    scan_kernel(In in, Out out, std::size_t n, Fold fold, unsigned* next, unsigned* flags, T* aggregate,
-                T* inclusive, std::uint64_t wait_ns) {
-  constexpr unsigned ROWS = scan_rows<T>();
-  constexpr std::size_t TILE = scan_tile<T>(), RUN = std::size_t(32) * ROWS;
+__global__ void __launch_bounds__(SCAN_BLOCK, SCAN_BLOCKS_PER_SM)
+    scan_kernel(In in, Out out, std::size_t n, Fold fold, unsigned* next, TileStates<T> st, std::uint64_t wait_ns) {
+  constexpr unsigned S = scan_segment<T>(), ROWS = S;  // each worker warp loads and writes S rows of 32
+  constexpr std::size_t TILE = scan_tile<T>();
+  extern __shared__ __align__(16) unsigned char scan_raw[];
+  T* vals = reinterpret_cast<T*>(scan_raw);                    // the tile, element e at e + e / S
+  T* seg = vals + TILE + SCAN_THREADS;                         // op over the tile before segment s, for each s
+  bool* seg_ok = reinterpret_cast<bool*>(seg + SCAN_THREADS);  // whether seg[s] holds anything
   __shared__ unsigned tile_id;
   __shared__ __align__(16) unsigned char totals_raw[SCAN_WARPS * sizeof(T)];
-  __shared__ __align__(16) unsigned char prefix_raw[(SCAN_WARPS + 1) * sizeof(T)];
-  __shared__ bool prefix_ok[SCAN_WARPS + 1];
+  __shared__ __align__(16) unsigned char prior_raw[sizeof(T)];
+  __shared__ bool prior_ok;
   T* totals = reinterpret_cast<T*>(totals_raw);
-  T* prefix = reinterpret_cast<T*>(prefix_raw);  // [w]: op over the tile's warps before w; [SCAN_WARPS]: the tile's
+  T& prior = *reinterpret_cast<T*>(prior_raw);  // op over every tile before this one
   const unsigned warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  auto at = [](std::size_t e) { return e + e / S; };
   if(threadIdx.x == 0) tile_id = atomicAdd(next, 1u);  // tiles in the order blocks start: predecessors are running
   __syncthreads();
-  const std::size_t t = tile_id, tile0 = t * TILE, run0 = tile0 + warp * RUN;
+  const std::size_t t = tile_id, tile0 = t * TILE;
+  const std::size_t valid = n - tile0 < TILE ? n - tile0 : TILE;  // elements of this tile inside the input
+  const bool full = valid == TILE;
 
-  T y[ROWS];
-#pragma unroll
-  for(unsigned r = 0; r < ROWS; ++r) {
-    const std::size_t i = run0 + r * 32 + lane;
-    y[r] = i < n ? T(in[i]) : T{};
+  if(warp == SCAN_WARPS) {  // the look-back warp: op over every tile before this one
+    Part<T> p{T{}, false};
+    if(t > 0) p = look_back<T>(in, t, TILE, fold, st, wait_ns, lane);
+    if(lane == 0) {
+      prior = p.v;
+      prior_ok = p.ok;
+    }
+    __syncthreads();  // (1) the prefix is ready; the workers have published the tile's aggregate
+    return;
   }
-  T carry{};
+
+  // load: this warp's rows w S .. w S + S - 1, coalesced, a second batch in flight while one is stored
+  {
+    T y[2][SCAN_LOAD_BATCH];
+    auto load = [&](T (&dst)[SCAN_LOAD_BATCH], unsigned r0) {
 #pragma unroll
-  for(unsigned r = 0; r < ROWS; ++r) {
-    const bool valid = run0 + r * 32 + lane < n;
+      for(unsigned r = 0; r < SCAN_LOAD_BATCH; ++r) {
+        const std::size_t e = (std::size_t(warp) * ROWS + r0 + r) * 32 + lane;
+        dst[r] = e < valid ? T(in[tile0 + e]) : T{};
+      }
+    };
+    auto store = [&](const T (&src)[SCAN_LOAD_BATCH], unsigned r0) {
+#pragma unroll
+      for(unsigned r = 0; r < SCAN_LOAD_BATCH; ++r) vals[at((std::size_t(warp) * ROWS + r0 + r) * 32 + lane)] = src[r];
+    };
+    load(y[0], 0);
+    if constexpr(ROWS == SCAN_LOAD_BATCH) {
+      store(y[0], 0);
+    } else {
+      static_assert(ROWS % (2 * SCAN_LOAD_BATCH) == 0, "batches in pairs");
+#pragma unroll 1
+      for(unsigned r0 = 0; r0 < ROWS; r0 += 2 * SCAN_LOAD_BATCH) {
+        load(y[1], r0 + SCAN_LOAD_BATCH);
+        store(y[0], r0);
+        if(r0 + 2 * SCAN_LOAD_BATCH < ROWS) load(y[0], r0 + 2 * SCAN_LOAD_BATCH);
+        store(y[1], r0 + SCAN_LOAD_BATCH);
+      }
+    }
+  }
+  __syncwarp();  // a thread's segment (S elements: S / 32 of its warp's rows) holds only rows its own warp loaded
+
+  // rake: this thread's segment, in order; its total
+  const std::size_t s0 = std::size_t(threadIdx.x) * S;
+  Part<T> mine{T{}, false};
+  if(full) {
+    T* v = vals + at(s0);  // a segment is contiguous in shared memory
+    T acc = v[0];
+#pragma unroll 16
+    for(unsigned j = 1; j < S; ++j) v[j] = acc = fold(acc, v[j]);
+    mine = Part<T>{acc, true};
+  } else {
+    for(unsigned j = 0; j < S && s0 + j < valid; ++j) {
+      T& v = vals[at(s0 + j)];
+      if(mine.ok) v = fold(mine.v, v);
+      mine = Part<T>{v, true};
+    }
+  }
+  // the segments before this one in the warp (an exclusive shuffle scan of the totals; lane - d holds earlier ones)
+  Part<T> before{T{}, false};
+  {
+    T w = mine.v;
+    bool ok = mine.ok;  // inclusive over lanes 0 .. lane
 #pragma unroll
     for(unsigned d = 1; d < 32; d <<= 1) {
-      const T o = shuffled(y[r], [&](unsigned w) { return __shfl_up_sync(~0u, w, d); });
-      if(lane >= d && valid) y[r] = fold(o, y[r]);
+      const T o = shuffled(w, [&](unsigned x) { return __shfl_up_sync(~0u, x, d); });
+      const bool ook = __shfl_up_sync(~0u, ok ? 1 : 0, d) && lane >= d;
+      if(ook) {
+        w = ok ? fold(o, w) : o;
+        ok = true;
+      }
     }
-    if(r > 0 && valid) y[r] = fold(carry, y[r]);
-    carry = shuffled(y[r], [&](unsigned w) { return __shfl_sync(~0u, w, 31); });
+    const T ex = shuffled(w, [&](unsigned x) { return __shfl_up_sync(~0u, x, 1); });
+    const bool ex_ok = __shfl_up_sync(~0u, ok ? 1 : 0, 1) && lane > 0;
+    before = Part<T>{ex, ex_ok};
+    if(lane == 31) totals[warp] = w;  // the warp's total (a warp with no valid element is never read)
   }
-  if(lane == 0) totals[warp] = carry;
-  __syncthreads();
+  workers_sync();  // every warp's total is in
 
-  if(warp == 0) {
-    const bool full = tile0 + TILE <= n;
-    Part<T> agg{T{}, false};
-    if(lane == 0) {
-      for(unsigned w = 0; w < SCAN_WARPS; ++w) {
-        prefix[w] = agg.v;
-        prefix_ok[w] = agg.ok;
-        // a run the input ends inside (or before) is the last that holds elements: its total is not needed
-        if(tile0 + (w + 1) * RUN <= n)
-          agg = agg.ok ? Part<T>{fold(agg.v, totals[w]), true} : Part<T>{totals[w], true};
-      }
-      if(full) {
-        if(t == 0) {
-          inclusive[0] = agg.v;
-          store_release(flags, TILE_PREFIX);
-        } else {
-          aggregate[t] = agg.v;
-          store_release(flags + t, TILE_AGGREGATE);
-        }
-      }
-    }
-    Part<T> before{T{}, false};
-    if(t > 0) before = look_back<T>(in, t, TILE, fold, flags, aggregate, inclusive, wait_ns, lane);
-    if(lane == 0) {
-      if(full && t > 0) {
-        inclusive[t] = before.ok ? fold(before.v, agg.v) : agg.v;
-        store_release(flags + t, TILE_PREFIX);
-      }
-      prefix[SCAN_WARPS] = before.v;
-      prefix_ok[SCAN_WARPS] = before.ok;
-    }
+  // the tile's aggregate, published at once for the tiles after this one
+  Part<T> agg{T{}, false};
+  if(threadIdx.x == 0) {
+    for(unsigned w = 0; w < SCAN_WARPS; ++w)  // warp w's segments hold elements only if its first one does
+      if(std::size_t(w) * 32 * S < valid) agg = agg.ok ? Part<T>{fold(agg.v, totals[w]), true} : Part<T>{totals[w], true};
+    if(full && t > 0) st.publish(t, TILE_AGGREGATE, agg.v);
   }
-  __syncthreads();
+  __syncthreads();  // (1) with the look-back warp: `prior` is known
+  if(threadIdx.x == 0 && full) st.publish(t, TILE_PREFIX, prior_ok ? fold(prior, agg.v) : agg.v);
 
-  // op over everything before this warp's run, then into each element
-  Part<T> q{prefix[SCAN_WARPS], prefix_ok[SCAN_WARPS]};
-  if(prefix_ok[warp]) q = q.ok ? Part<T>{fold(q.v, prefix[warp]), true} : Part<T>{prefix[warp], true};
-  if(q.ok) {
-#pragma unroll
-    for(unsigned r = 0; r < ROWS; ++r)
-      if(run0 + r * 32 + lane < n) y[r] = fold(q.v, y[r]);
+  // this segment's prefix: the tiles before, the warps before, the segments before in this warp
+  {
+    Part<T> q{prior, prior_ok};
+    for(unsigned w = 0; w < warp; ++w) q = q.ok ? Part<T>{fold(q.v, totals[w]), true} : Part<T>{totals[w], true};
+    if(before.ok) q = q.ok ? Part<T>{fold(q.v, before.v), true} : before;
+    seg[threadIdx.x] = q.v;
+    seg_ok[threadIdx.x] = q.ok;
   }
-#pragma unroll
+  workers_sync();
+
+  // write: this warp's rows again, each element with its segment's prefix
   for(unsigned r = 0; r < ROWS; ++r) {
-    const std::size_t i = run0 + r * 32 + lane;
-    if constexpr(Exclusive) {
-      const T up = shuffled(y[r], [&](unsigned w) { return __shfl_up_sync(~0u, w, 1); });
-      const T last = shuffled(r ? y[r - 1] : y[0], [&](unsigned w) { return __shfl_sync(~0u, w, 31); });
-      if(i < n) out[i] = lane ? up : (r ? last : (q.ok ? q.v : T{}));
+    const std::size_t e = (std::size_t(warp) * ROWS + r) * 32 + lane;
+    if(e >= valid) break;
+    if constexpr(Exclusive) {  // the inclusive prefix of the element before
+      if(e == 0) {
+        out[tile0] = prior_ok ? prior : T{};
+      } else {
+        const std::size_t p = e - 1, s = p / S;
+        const T v = vals[at(p)];
+        out[tile0 + e] = seg_ok[s] ? fold(seg[s], v) : v;
+      }
     } else {
-      if(i < n) out[i] = y[r];
+      const std::size_t s = e / S;
+      const T v = vals[at(e)];
+      out[tile0 + e] = seg_ok[s] ? fold(seg[s], v) : v;
     }
   }
 }
 
-// The scan's scratch: the tile counter, one state word per tile, then each tile's aggregate and inclusive prefix.
+// The scan's scratch: the tile counter, then one 64-bit state-and-value word per tile (values of four bytes or
+// fewer), or one state word per tile and each tile's aggregate and inclusive prefix (larger values).
+template<class T> inline std::size_t scan_tiles(std::size_t n) noexcept { return (n + scan_tile<T>() - 1) / scan_tile<T>(); }
+template<class T> inline std::size_t scan_head_bytes(std::size_t n) noexcept {
+  return 256 + round256(scan_tiles<T>(n) * (TileStates<T>::PACKED ? 8 : 4));
+}
 template<class T> inline std::size_t scan_scratch_bytes(std::size_t n) noexcept {
-  const std::size_t tiles = (n + scan_tile<T>() - 1) / scan_tile<T>();
-  return 256 + round256(tiles * 4) + 2 * round256(tiles * sizeof(T));
+  return scan_head_bytes<T>(n) + (TileStates<T>::PACKED ? 0 : 2 * round256(scan_tiles<T>(n) * sizeof(T)));
 }
 
 template<bool Exclusive, class T, class In, class Out, class Fold>
@@ -309,17 +465,26 @@ void scan(void* temp, std::size_t& bytes, In in, Out out, std::size_t n, Fold fo
     return;
   }
   if(!n) return;
-  const std::size_t tiles = (n + scan_tile<T>() - 1) / scan_tile<T>();
+  const std::size_t tiles = scan_tiles<T>(n);
   if(tiles > 0x7fffffffull) trap();
   char* base = static_cast<char*>(temp);
-  const std::size_t head = 256 + round256(tiles * 4), cells = round256(tiles * sizeof(T));
-  unsigned* next = reinterpret_cast<unsigned*>(base);
-  unsigned* flags = reinterpret_cast<unsigned*>(base + 256);
-  T* aggregate = reinterpret_cast<T*>(base + head);
-  T* inclusive = reinterpret_cast<T*>(base + head + cells);
+  const std::size_t head = scan_head_bytes<T>(n), cells = round256(tiles * sizeof(T));
+  TileStates<T> st{};
+  st.words = reinterpret_cast<unsigned long long*>(base + 256);
+  st.flags = reinterpret_cast<unsigned*>(base + 256);
+  st.aggregate = reinterpret_cast<T*>(base + head);
+  st.inclusive = reinterpret_cast<T*>(base + head + cells);
+  static const bool sized = [] {  // the tile's dynamic shared memory, above the 48 KB default
+    check(cudaFuncSetAttribute(scan_kernel<Exclusive, T, In, Out, Fold>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize, int(scan_smem<T>())));
+    check(cudaFuncSetAttribute(scan_kernel<Exclusive, T, In, Out, Fold>,
+                               cudaFuncAttributePreferredSharedMemoryCarveout, 100));  // room for three tiles
+    return true;
+  }();
+  (void)sized;
   check(cudaMemsetAsync(base, 0, head, s));  // the counter and every tile's state start at zero
-  scan_kernel<Exclusive, T><<<unsigned(tiles), SCAN_THREADS, 0, s>>>(in, out, n, fold, next, flags, aggregate,
-                                                                     inclusive, wait_ns);
+  scan_kernel<Exclusive, T><<<unsigned(tiles), SCAN_BLOCK, scan_smem<T>(), s>>>(
+      in, out, n, fold, reinterpret_cast<unsigned*>(base), st, wait_ns);
   check(cudaGetLastError());
 }
 

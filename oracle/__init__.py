@@ -145,6 +145,20 @@ class restated:
         return out
 
     @staticmethod
+    def scan_u32(x: np.ndarray) -> tuple[np.ndarray, int]:
+        x = np.ascontiguousarray(x, np.uint32)
+        out = np.empty_like(x)
+        total = _rest.fn("scan_u32", C.c_uint32, [_z, _p, _p])(x.size, _ptr(out), _ptr(x))
+        return out, int(total)
+
+    @staticmethod
+    def runmax_i32(x: np.ndarray) -> tuple[np.ndarray, int]:
+        x = np.ascontiguousarray(x, np.int32)
+        out = np.empty_like(x)
+        total = _rest.fn("runmax_i32", C.c_int32, [_z, _p, _p])(x.size, _ptr(out), _ptr(x))
+        return out, int(total)
+
+    @staticmethod
     def widen(fmt: str, bits: np.ndarray) -> np.ndarray:
         name = {"bf16": "bf16_to_f32", "f16": "f16_to_f32", "f8e4m3": "e4m3_to_f32", "f8e5m2": "e5m2_to_f32"}[fmt]
         argt = C.c_uint16 if fmt in ("bf16", "f16") else C.c_uint8
@@ -205,6 +219,20 @@ class reference:
         out = np.empty_like(x) if out is None else out
         _ref.fn("saxpy_f32", None, [_z, _p, _p, _p, _f])(x.size, _ptr(out), _ptr(x), _ptr(y), a)
         return out
+
+    @staticmethod
+    def scan_u32(x: np.ndarray, out: np.ndarray | None = None) -> tuple[np.ndarray, int]:
+        x = np.ascontiguousarray(x, np.uint32)
+        out = np.empty_like(x) if out is None else out
+        total = _ref.fn("scan_u32", C.c_uint32, [_z, _p, _p])(x.size, _ptr(out), _ptr(x))
+        return out, int(total)
+
+    @staticmethod
+    def runmax_i32(x: np.ndarray) -> tuple[np.ndarray, int]:
+        x = np.ascontiguousarray(x, np.int32)
+        out = np.empty_like(x)
+        total = _ref.fn("runmax_i32", C.c_int32, [_z, _p, _p])(x.size, _ptr(out), _ptr(x))
+        return out, int(total)
 
     @staticmethod
     def widen(fmt: str, bits: np.ndarray) -> np.ndarray:

@@ -16,6 +16,10 @@
  *                         overflow flag that is set exactly when the true total does not fit.
  *   - oracle_saxpy_f32    cr::gpu::run / cr::par::run of out[i] = a * x[i] + y[i] (runtime/cairn_exec.hpp:103-108,
  *                         cairn_parallel.hpp:372-378): two roundings, no fused multiply-add.
+ *   - oracle_scan_u32     cr::par::scan<false> (runtime/cairn_parallel.hpp:401-440) of add_wrap over u32: the
+ *                         inclusive prefixes modulo 2^32 in index order, and the total.
+ *   - oracle_runmax_i32   cr::par::scan<true> of max over i32: out[0] = INT32_MIN, out[i] = max(x[0..i)), and the
+ *                         total max(x[0..n)).
  *   - oracle_bias_act     the fused epilogue this project adds beside the multiply (the reference has none,
  *                         cairn_tensor.hpp:189-193 only stores the f32 accumulator): bf16(act(f32(acc + bias[j]))).
  *   - oracle_gemm_t16     the transposed products the derive-grad backward of a dense layer forms
@@ -258,6 +262,21 @@ uint64_t oracle_sum_u64(size_t n, const uint64_t* x, int* overflow) {
 }
 
 /* out[i] = f32(f32(a * x[i]) + y[i]) */
+uint32_t oracle_scan_u32(size_t n, uint32_t* out, const uint32_t* x) {
+  uint32_t acc = 0;
+  for (size_t i = 0; i < n; ++i) out[i] = acc = acc + x[i];
+  return acc;
+}
+
+int32_t oracle_runmax_i32(size_t n, int32_t* out, const int32_t* x) {
+  int32_t acc = INT32_MIN;
+  for (size_t i = 0; i < n; ++i) {
+    out[i] = acc;
+    if (x[i] > acc) acc = x[i];
+  }
+  return acc;
+}
+
 void oracle_saxpy_f32(size_t n, float* out, const float* x, const float* y, float a) {
   for (size_t i = 0; i < n; ++i) {
     volatile float p = a * x[i];

@@ -16,6 +16,9 @@
 //                        (runtime/cairn_runtime.hpp:158-166): the checked sum, with its overflow flag returned
 //                        instead of trapping.
 //   ref_saxpy_f32        cr::par::run of out[i] = a * x[i] + y[i].
+//   ref_scan_u32         cr::par::scan<false> (runtime/cairn_parallel.hpp:401-440) of `scan add_wrap parallel i
+//                        in n yield x[i]` over u32: inclusive prefixes modulo 2^32, returning the total.
+//   ref_runmax_i32       cr::par::scan<true> of `scan exclusive max` over i32 from the identity INT32_MIN.
 //   ref_narrow_*/ref_widen_*  cr::fp::narrow and the storage floats' exact widening (runtime/cairn_float.hpp).
 #include <cstddef>
 #include <cstdint>
@@ -75,6 +78,17 @@ std::uint64_t ref_sum_u64(std::size_t n, const std::uint64_t* x, int* overflow) 
 
 void ref_saxpy_f32(std::size_t n, float* out, const float* x, const float* y, float a) {
   cr::par::run(n, [=](std::size_t i) noexcept { out[i] = a * x[i] + y[i]; });
+}
+
+std::uint32_t ref_scan_u32(std::size_t n, std::uint32_t* out, const std::uint32_t* x) {
+  return cr::par::scan<false, std::uint32_t>(
+      out, n, 0u, [](std::uint32_t p, std::uint32_t q) noexcept { return cr::add_wrap(p, q); },
+      [x](std::size_t i) noexcept { return x[i]; });
+}
+std::int32_t ref_runmax_i32(std::size_t n, std::int32_t* out, const std::int32_t* x) {
+  return cr::par::scan<true, std::int32_t>(
+      out, n, std::int32_t(-2147483647 - 1), [](std::int32_t p, std::int32_t q) noexcept { return p < q ? q : p; },
+      [x](std::size_t i) noexcept { return x[i]; });
 }
 
 std::uint16_t ref_narrow_bf16(double x) { return cr::fp::narrow<cr::bf16>(x).bits; }

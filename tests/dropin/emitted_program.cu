@@ -1,7 +1,7 @@
 // A CAIRN device library in the form cairnc emits it (compiler/lower/codegen.py:438-446 for the checked cf_ entries,
 // compiler/lower/header.py:230-247 for the enqueued cq_ entries, compiler/lower/region_lowering.py:122-183 and
 // compiler/device/tensor.py:69-82 for the bodies): every function's body calls only the runtime's templates,
-// cr::gpu::run, cr::gpu::run_vector, cr::gpu::reduce_on, cr::gpu::scan_on, cr::gpu::compact_on and cr::tensor::launch. It is built against the CAIRN
+// cr::gpu::run, cr::gpu::run_vector, cr::gpu::run_staged, cr::gpu::reduce_on, cr::gpu::scan_on, cr::gpu::compact_on and cr::tensor::launch. It is built against the CAIRN
 // runtime headers with include/cairn_b200/runtime ahead of them on the include path (tests/dropin/build_emitted.py),
 // so the same source runs on the B200 machine and libcairn_b200.so. Test input of tests/test_dropin_gpu.py.
 #include <cstddef>
@@ -96,6 +96,38 @@ std::size_t ci_positives(std::size_t n, float* out, const float* x) {
       cr::gpu::here(), out, n, [=] CR_DEVICE(std::size_t i) { return x[i] > 0.0f; },
       [=] CR_DEVICE(std::size_t i) { return x[i]; });
 }
+// fn blur(n: usize, out: rw<f32>[n]@device, x: ro<f32>[n]@device) {
+//   parallel i in n {
+//     if i >= 2 && i + 2 < n { out[i] = x[i - 2] + x[i - 1] * 2.0 + x[i] * 3.0 + x[i + 1] + x[i + 2]; }
+//     else { out[i] = x[i]; }
+//   }
+// }
+// plan blur { stage 2; block 128; }   (compiler/plans/staging.py:95-122 emits the three lambdas this way)
+void ci_blur(std::size_t n, float* out, const float* x) {
+  cr::gpu::run_staged<2>(
+      cr::gpu::here(), n,
+      [=] CR_DEVICE(std::size_t cr_base, std::size_t cr_w, std::size_t cr_t, std::size_t cr_b,
+                    unsigned char* cr_shared) {
+        float* const cr_s_x = reinterpret_cast<float*>(cr_shared + 0);
+        for(std::size_t cr_e = cr_t; cr_e < cr_w; cr_e += cr_b) {
+          const std::size_t cr_g = cr_base + cr_e;  // element cr_g - 2, loaded only inside the array
+          if(cr_g >= 2 && cr_g - 2 < n) cr_s_x[cr_e] = x[cr_g - 2];
+        }
+      },
+      [=] CR_DEVICE(std::size_t v_i, std::size_t cr_base, std::size_t cr_w, unsigned char* cr_shared) {
+        const float* const cr_s_x = reinterpret_cast<const float*>(cr_shared + 0);
+        const std::size_t o = v_i - cr_base + 2;  // x[i + d] is cr_s_x[o + d]
+        if(v_i >= 2 && v_i + 2 < n)
+          out[v_i] = cr_s_x[o - 2] + cr_s_x[o - 1] * 2.0f + cr_s_x[o] * 3.0f + cr_s_x[o + 1] + cr_s_x[o + 2];
+        else
+          out[v_i] = cr_s_x[o];
+      },
+      [](std::size_t cr_w) { return cr::gpu::tile_bytes<float>(cr_w); }, 128);
+}
+struct WrapAdd {
+  CR_DEVICE std::uint32_t operator()(std::uint32_t p, std::uint32_t q) const { return cr::add_wrap(p, q); }
+};
+inline const std::uint32_t* x_none() { return nullptr; }
 }  // namespace
 
 extern "C" {
@@ -176,5 +208,32 @@ void cf_prefix_escape(std::size_t n, std::uint64_t* out, const std::uint64_t* x)
   cr::gpu::b200::scan<false, std::uint64_t>(temp, bytes, x, out, n, cr::gpu::b200::Plus{}, nullptr, 0);
   cr::gpu::check(cudaStreamSynchronize(nullptr));
   cr::gpu::check(cudaFree(temp));
+}
+void cf_blur(std::size_t n, float* out, const float* x) noexcept {
+  cr::view(out, n);
+  cr::view(x, n);
+  ci_blur(n, out, x);
+}
+// pub fn wscan(n, out: rw<u32>[n]@device, x: ro<u32>[n]@device)
+//   { scan add_wrap parallel i in n yield x[i] into out; }   (no total: scan_into, enqueued on the caller's stream)
+void cq_wscan(void* stream, std::size_t n, std::uint32_t* out, const std::uint32_t* x) noexcept {
+  cr::view(out, n);
+  cr::view(x, n);
+  cr::gpu::Enqueued queued(stream);
+  cr::gpu::scan_into<false, std::uint32_t>(
+      cr::gpu::here(), out, n, 0u, [] CR_DEVICE(std::uint32_t p, std::uint32_t q) { return cr::add_wrap(p, q); },
+      [=] CR_DEVICE(std::size_t i) { return x[i]; });
+}
+// Not cairnc entries: the machine's inclusive u32 add_wrap scan kernel alone, on the caller's stream and scratch
+// (b200_scan_u32_scratch bytes), so a bench can time the kernel without the context's copy pass.
+std::size_t b200_scan_u32_scratch(std::size_t n) noexcept {
+  std::size_t bytes = 0;
+  cr::gpu::b200::scan<false, std::uint32_t>(nullptr, bytes, x_none(), static_cast<std::uint32_t*>(nullptr), n,
+                                            WrapAdd{}, nullptr);
+  return bytes;
+}
+void b200_scan_u32(void* stream, std::size_t n, std::uint32_t* out, const std::uint32_t* x, void* temp) noexcept {
+  std::size_t bytes = b200_scan_u32_scratch(n);
+  cr::gpu::b200::scan<false, std::uint32_t>(temp, bytes, x, out, n, WrapAdd{}, static_cast<cudaStream_t>(stream));
 }
 }

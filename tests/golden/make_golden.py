@@ -13,6 +13,8 @@ GPU box, and give the GPU parity tests the reference's own answers for the cases
              config 1) and overflow cases
   saxpy.npz  cr::par::run of out = a * x + y
   f32gemm.npz  the `parallel e in m*n` f32 GEMM region of BASELINE config 1, at a reduced size
+  scan.npz   cr::par::scan: inclusive add_wrap over u32 and exclusive max over i32, on sizes around the device
+             scan's tiles (4096 four-byte elements) and with wrapping totals
 """
 
 from __future__ import annotations
@@ -80,10 +82,27 @@ def f32gemm() -> dict:
     return {"a": a, "b": b, "shape": np.asarray([m, n, k]), "want": reference.gemm_f32_region(c, a, b, m, n, k)}
 
 
+SCAN_SIZES = (1, 2, 4095, 4096, 4097, 8193)
+
+
+def scan() -> dict:
+    out = {}
+    for n in SCAN_SIZES:
+        rng = np.random.default_rng(n)
+        x = rng.integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
+        got, total = reference.scan_u32(x)
+        out[f"u32/{n}/x"], out[f"u32/{n}/want"], out[f"u32/{n}/total"] = x, got, np.asarray([total], np.uint32)
+        v = rng.integers(-2**31, 2**31 - 1, n, dtype=np.int64).astype(np.int32)
+        got, total = reference.runmax_i32(v)
+        out[f"max/{n}/x"], out[f"max/{n}/want"], out[f"max/{n}/total"] = v, got, np.asarray([total], np.int32)
+    return out
+
+
 def main() -> None:
     if not reference.available():
         raise SystemExit("oracle/_ref/libcairn_ref.so is not built: make -C oracle REF=<cairn>/src/cairn/runtime")
-    for name, fn in (("mma", mma), ("sum", sums), ("u64", u64), ("saxpy", saxpy), ("f32gemm", f32gemm)):
+    for name, fn in (("mma", mma), ("sum", sums), ("u64", u64), ("saxpy", saxpy), ("f32gemm", f32gemm),
+                     ("scan", scan)):
         np.savez_compressed(HERE / f"{name}.npz", **fn())
         print(f"wrote {name}.npz")
 

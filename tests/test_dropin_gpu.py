@@ -40,7 +40,9 @@ def emitted(cuda):
                             ("cf_gemm", None, [z, z, z, z, p, z, p, z, p]), ("cf_prefix", C.c_uint64, [z, p, p]),
                             ("cf_wprefix", C.c_uint32, [z, p, p]), ("cf_runmax", C.c_int32, [z, p, p]),
                             ("cf_fprefix", C.c_float, [z, p, p]), ("cf_positives", C.c_size_t, [z, p, p]),
-                            ("cf_prefix_escape", None, [z, p, p])):
+                            ("cf_prefix_escape", None, [z, p, p]), ("cf_blur", None, [z, p, p]),
+                            ("cq_wscan", None, [p, z, p, p]), ("b200_scan_u32_scratch", z, [z]),
+                            ("b200_scan_u32", None, [p, z, p, p, p])):
         f = getattr(h, name)
         f.restype, f.argtypes = res, args
     return h
@@ -114,15 +116,49 @@ def test_emitted_integer_scans(emitted, cuda, n):
     w = rng.integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
     wt, wout = _dev(w.view(np.int32), cuda), torch.empty(n, dtype=torch.int32, device=cuda)
     wtotal = emitted.cf_wprefix(n, wout.data_ptr(), wt.data_ptr())
-    wwant = np.cumsum(w, dtype=np.uint32)  # add_wrap: modulo 2^32
-    assert np.array_equal(wout.cpu().numpy().view(np.uint32), wwant) and wtotal == int(wwant[-1])
+    wwant, wwant_total = restated.scan_u32(w)  # add_wrap: modulo 2^32
+    assert np.array_equal(wout.cpu().numpy().view(np.uint32), wwant) and wtotal == wwant_total
 
     v = rng.integers(-2**31, 2**31 - 1, n, dtype=np.int64).astype(np.int32)
     vt, vout = _dev(v, cuda), torch.empty(n, dtype=torch.int32, device=cuda)
     vtotal = emitted.cf_runmax(n, vout.data_ptr(), vt.data_ptr())
-    run = np.maximum.accumulate(v)
-    want_ex = np.concatenate([[np.int32(-2**31)], run[:-1]]).astype(np.int32)
-    assert np.array_equal(vout.cpu().numpy(), want_ex) and vtotal == int(run[-1])
+    vwant, vwant_total = restated.runmax_i32(v)
+    assert np.array_equal(vout.cpu().numpy(), vwant) and vtotal == vwant_total
+
+
+def test_emitted_scans_against_the_reference_fixture(emitted, cuda):
+    d = np.load(Path(__file__).resolve().parent / "golden" / "scan.npz")
+    for n in sorted({int(k.split("/")[1]) for k in d.files}):
+        x = d[f"u32/{n}/x"]
+        out = torch.empty(n, dtype=torch.int32, device=cuda)
+        total = emitted.cf_wprefix(n, out.data_ptr(), _dev(x.view(np.int32), cuda).data_ptr())
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), d[f"u32/{n}/want"])
+        assert total == int(d[f"u32/{n}/total"][0])
+        v = d[f"max/{n}/x"]
+        vout = torch.empty(n, dtype=torch.int32, device=cuda)
+        vtotal = emitted.cf_runmax(n, vout.data_ptr(), _dev(v, cuda).data_ptr())
+        assert np.array_equal(vout.cpu().numpy(), d[f"max/{n}/want"]) and vtotal == int(d[f"max/{n}/total"][0])
+
+
+def test_enqueued_scan_and_the_machine_kernel_alone(emitted, cuda):
+    """cq_wscan (scan_into on the caller's stream) and the machine's scan kernel called directly give the oracle's
+    prefixes."""
+    n = 3 * 4096 * 37 + 11
+    x = np.random.default_rng(5).integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
+    want, _ = restated.scan_u32(x)
+    xt = _dev(x.view(np.int32), cuda)
+    s = torch.cuda.Stream(cuda)
+    out = torch.empty(n, dtype=torch.int32, device=cuda)
+    with torch.cuda.stream(s):
+        emitted.cq_wscan(s.cuda_stream, n, out.data_ptr(), xt.data_ptr())
+    s.synchronize()
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want)
+    temp = torch.empty(emitted.b200_scan_u32_scratch(n), dtype=torch.uint8, device=cuda)
+    raw = torch.empty(n, dtype=torch.int32, device=cuda)
+    emitted.b200_scan_u32(torch.cuda.current_stream(cuda).cuda_stream, n, raw.data_ptr(), xt.data_ptr(),
+                          temp.data_ptr())
+    torch.cuda.synchronize()
+    assert np.array_equal(raw.cpu().numpy().view(np.uint32), want)
 
 
 @pytest.mark.parametrize("n", [1, 4097, 1_000_003])
@@ -158,3 +194,57 @@ def test_scan_look_back_escape_gives_the_same_prefixes(emitted, cuda, n):
     out = torch.empty(n, dtype=torch.int64, device=cuda)
     emitted.cf_prefix_escape(n, out.data_ptr(), _dev(x.view(np.int64), cuda).data_ptr())
     assert np.array_equal(out.cpu().numpy().view(np.uint64), np.cumsum(x, dtype=np.uint64))
+
+
+@pytest.mark.parametrize("n", [1, 4, 5, 127, 128, 129, 131, 100_003])
+def test_emitted_staged_region(emitted, cuda, n):
+    """`plan blur { stage 2; block 128; }`: every tile a block loads holds what its lanes read, at the array's edges
+    and between blocks; the body's f32 arithmetic in source order (--fmad=false), bit for bit."""
+    x = np.random.default_rng(n + 4).uniform(-1, 1, n).astype(np.float32)
+    out = torch.empty(n, dtype=torch.float32, device=cuda)
+    emitted.cf_blur(n, out.data_ptr(), _dev(x, cuda).data_ptr())
+    want = x.copy()
+    if n >= 5:
+        two, three = np.float32(2.0), np.float32(3.0)
+        mid = x[:-4] + x[1:-3] * two
+        mid = mid + x[2:-2] * three
+        mid = mid + x[3:-1]
+        want[2:-2] = mid + x[4:]
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want.view(np.uint32))
+
+
+def test_machine_scan_many_look_back_windows_against_the_oracle(emitted, cuda):
+    """2^27 u32 values: 8,192 tiles, so look-backs cross many 128-tile windows while others are still in flight."""
+    n = 1 << 27
+    x = np.random.default_rng(27).integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
+    want, total = restated.scan_u32(x)
+    out = torch.empty(n, dtype=torch.int32, device=cuda)
+    got_total = emitted.cf_wprefix(n, out.data_ptr(), _dev(x.view(np.int32), cuda).data_ptr())
+    assert got_total == total
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want)
+
+
+@pytest.mark.slow
+def test_machine_scan_at_the_bench_size_by_differences(emitted, cuda):
+    """n = 2^30 (the bench's size): out[0] = x[0] and out[i] - out[i - 1] = x[i] modulo 2^32 at every i, checked on
+    the device, through both the enqueued entry and the machine's kernel alone."""
+    n = 1 << 30
+    g = torch.Generator(device=cuda).manual_seed(30)
+    x = torch.randint(-2**31, 2**31 - 1, (n,), device=cuda, dtype=torch.int32, generator=g)
+    out = torch.empty_like(x)
+
+    def holds() -> bool:
+        ok = bool(out[0] == x[0])
+        for lo in range(1, n, 1 << 28):  # int32 differences wrap like add_wrap's u32 sums
+            hi = min(n, lo + (1 << 28))
+            ok = ok and bool(((out[lo:hi] - out[lo - 1:hi - 1]) == x[lo:hi]).all())
+        return ok
+
+    emitted.cq_wscan(torch.cuda.current_stream(cuda).cuda_stream, n, out.data_ptr(), x.data_ptr())
+    torch.cuda.synchronize()
+    assert holds()
+    out.zero_()
+    temp = torch.empty(emitted.b200_scan_u32_scratch(n), dtype=torch.uint8, device=cuda)
+    emitted.b200_scan_u32(torch.cuda.current_stream(cuda).cuda_stream, n, out.data_ptr(), x.data_ptr(), temp.data_ptr())
+    torch.cuda.synchronize()
+    assert holds()

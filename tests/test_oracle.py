@@ -60,6 +60,17 @@ def test_restated_saxpy_equals_the_reference_fixture():
     assert np.array_equal(got.view(np.uint32), d["want"].view(np.uint32))
 
 
+def test_restated_scans_equal_the_reference_fixture():
+    d = np.load(GOLDEN / "scan.npz")
+    sizes = sorted({int(k.split("/")[1]) for k in d.files})
+    assert sizes, "scan.npz holds no cases"
+    for n in sizes:
+        got, total = restated.scan_u32(d[f"u32/{n}/x"])
+        assert np.array_equal(got, d[f"u32/{n}/want"]) and total == int(d[f"u32/{n}/total"][0]), n
+        got, total = restated.runmax_i32(d[f"max/{n}/x"])
+        assert np.array_equal(got, d[f"max/{n}/want"]) and total == int(d[f"max/{n}/total"][0]), n
+
+
 def test_restated_f32_region_gemm_equals_the_reference_fixture():
     d = np.load(GOLDEN / "f32gemm.npz")
     m, n, k = map(int, d["shape"])
@@ -121,6 +132,19 @@ def test_restated_sums_equal_the_reference_live():
 
 
 @needs_ref
+def test_restated_scans_equal_the_reference_live():
+    if not reference.available():
+        pytest.skip("oracle/_ref is not built (it needs the CAIRN reference tree)")
+    rng = np.random.default_rng(21)
+    for n in (1, 4097, 250_003):
+        x = rng.integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
+        a, b = restated.scan_u32(x), reference.scan_u32(x)
+        assert np.array_equal(a[0], b[0]) and a[1] == b[1]
+        v = rng.integers(-2**31, 2**31 - 1, n, dtype=np.int64).astype(np.int32)
+        a, b = restated.runmax_i32(v), reference.runmax_i32(v)
+        assert np.array_equal(a[0], b[0]) and a[1] == b[1]
+
+
 def test_restated_widening_and_saxpy_equal_the_reference_live():
     for fmt in inputs.FORMATS:
         bits = np.arange(256, dtype=np.uint8 if inputs.WIDTH[fmt] == 8 else np.uint16)
