@@ -326,27 +326,25 @@ class Gemm:
             raise SystemExit(f"cairn_b200_gemm failed with status {st}")
 
     def e2e(self, steps: int, warmup: int):
-        """The same product through the C ABI from pinned host memory: A, B and bias copied in, the bf16 (or f32)
-        result copied out, every step."""
+        """The same product from pinned host memory through cairn_b200.HostGemm (the library's host-buffer multiply:
+        B, bias and A's row chunks copied in, each chunk's rows of C computed as they land and copied back), every
+        step's operands in and its whole bf16 (or f32) result out; steps overlap as a stream of products would."""
         torch = self.torch
+        from cairn_b200 import HostGemm
+
         a_h = [self.a[s].cpu().pin_memory() for s in range(2)]
         b_h = self.b[0].cpu().pin_memory()
-        bias_h = self.bias.cpu().pin_memory()
+        bias_h = None if self.config5 else self.bias.cpu().pin_memory()
         out_h = torch.empty(self.out[0].shape, dtype=self.out[0].dtype).pin_memory()
-        a_d, b_d, bias_d, out_d = self.a[0], self.b[0], self.bias, self.out[0]
-        lib, st = self.lib, self.stream.cuda_stream
-        kind, bias_p, act = (1, None, 0) if self.config5 else (2, bias_d.data_ptr(), 1)
+        hg = HostGemm(self.m, self.n, self.k, out_dtype=self.out[0].dtype, bias=not self.config5,
+                      device=self.dist.device)
 
         def step(i):
-            a_d.copy_(a_h[i % 2], non_blocking=True)
-            b_d.copy_(b_h, non_blocking=True)
-            bias_d.copy_(bias_h, non_blocking=True)
-            check(lib.cairn_b200_gemm(st, 0, self.m, self.n, self.k, a_d.data_ptr(), 0, b_d.data_ptr(), 0,
-                                      out_d.data_ptr(), kind, bias_p, act), "gemm")
-            out_h.copy_(out_d, non_blocking=True)
+            done = hg.submit(a_h[i % 2], b_h, out_h, bias_h, relu=not self.config5)
+            self.stream.wait_event(done)  # the timed region ends when the last result is in host memory
 
         ms, _, _, _ = time_steps(self.dist, self.stream, step, steps, warmup, per_launch=False)
-        h2d = a_h[0].numel() * 2 + b_h.numel() * 2 + bias_h.numel() * 4
+        h2d = a_h[0].numel() * 2 + b_h.numel() * 2 + (bias_h.numel() * 4 if bias_h is not None else 0)
         d2h = out_h.numel() * out_h.element_size()
         return self.dist.world * self.flops / (ms * 1e-3) / 1e12, h2d, d2h
 
@@ -411,15 +409,14 @@ class Stream:
         chunk = min(self.n, 1 << 26)  # the e2e sample: 2^26 elements per rank from pinned host memory
         x_h = self.x[:chunk].cpu().pin_memory()
         x_d = self.x[:chunk]
-        if self.workload == "saxpy":
+        if self.workload == "saxpy":  # through cairn_b200.HostSaxpy: copies in, regions and copies out overlapped
+            from cairn_b200 import HostSaxpy
+
             y_h, o_h = self.y[:chunk].cpu().pin_memory(), torch.empty(chunk, dtype=torch.float32).pin_memory()
-            y_d, o_d = self.y[:chunk], self.o[:chunk]
+            hs = HostSaxpy(chunk, device=self.dist.device)
 
             def step(i):
-                x_d.copy_(x_h, non_blocking=True)
-                y_d.copy_(y_h, non_blocking=True)
-                check(lib.cairn_b200_saxpy_f32(st, chunk, o_d.data_ptr(), x_d.data_ptr(), y_d.data_ptr(), 2.5), "saxpy")
-                o_h.copy_(o_d, non_blocking=True)
+                self.stream.wait_event(hs.submit(2.5, x_h, y_h, o_h))
 
             h2d, d2h = 8 * chunk, 4 * chunk
         else:
@@ -519,17 +516,16 @@ class Mlp:
         self.mlp.mlp_step(self.x, self.w1, self.w2, self.t, self.ws, self.stream.cuda_stream)
 
     def e2e(self, steps: int, warmup: int):
-        """The step through the C ABI with this step's batch and target copied in from pinned host memory and the
-        loss read back; the weights stay resident as in training."""
+        """The step through mlp.step_from_host: this step's batch and target copied in from pinned host memory (on the
+        feed's stream, while the step before computes) and the loss read back; the weights stay resident as in
+        training."""
         torch = self.torch
         x_h, t_h = self.x.cpu().pin_memory(), self.t.cpu().pin_memory()
         loss_h = torch.empty(1, dtype=torch.float32).pin_memory()
+        feed = self.mlp.HostFeed(self.B, self.D, self.O, self.dist.device)
 
         def step(i):
-            self.x.copy_(x_h, non_blocking=True)
-            self.t.copy_(t_h, non_blocking=True)
-            self.launch(i)
-            loss_h.copy_(self.ws.loss, non_blocking=True)
+            self.mlp.step_from_host(feed, x_h, t_h, self.w1, self.w2, self.ws, loss_h, self.stream)
 
         ms, _, _, _ = time_steps(self.dist, self.stream, step, steps, warmup, per_launch=False)
         return self.dist.world * self.flops / (ms * 1e-3) / 1e12, x_h.numel() * 2 + t_h.numel() * 4, 4

@@ -6,10 +6,13 @@ torch-facing forms of its entries (cairn_b200.ops) and the range-sharded multi-G
 """
 
 from ._lib import CairnError, LIB_PATH, header_symbols, lib
+from .host import HostGemm, HostSaxpy
 from .ops import gemm, mma_unordered, reduce_sum, saxpy, stream_status, watchdog_selftest
 
 __all__ = [
     "CairnError",
+    "HostGemm",
+    "HostSaxpy",
     "LIB_PATH",
     "gemm",
     "header_symbols",

@@ -64,6 +64,54 @@ def mlp_step(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, t: torch.Tenso
     return ws
 
 
+class HostFeed:
+    """Batches from pinned host memory for a run of steps. Each batch (x, t) is copied on the feed's own stream into
+    one of `depth` device buffer sets while the step before computes from another, so a training loop's input copies
+    overlap its products instead of preceding them; a set is refilled only after the step that read it has run."""
+
+    def __init__(self, batch: int, d_in: int, d_out: int, device: torch.device, depth: int = 2):
+        self.sets = [[torch.empty(batch, d_in, dtype=torch.bfloat16, device=device),
+                      torch.empty(batch, d_out, dtype=torch.float32, device=device), None] for _ in range(depth)]
+        self.copy = torch.cuda.Stream(device)
+        self.calls = 0
+
+    def put(self, x_host: torch.Tensor, t_host: torch.Tensor):
+        """Queues the batch's copies; returns (x, t, ready, slot): the device tensors, the event that marks them
+        copied, and the slot to hand back to `done`."""
+        slot = self.calls % len(self.sets)
+        self.calls += 1
+        x, t, free = self.sets[slot]
+        if x_host.shape != x.shape or t_host.shape != t.shape or x_host.dtype != x.dtype or t_host.dtype != t.dtype:
+            raise CairnError(ERR_ARG, "HostFeed.put: x and t of the feed's shapes (x bf16, t f32)")
+        if free is not None:
+            self.copy.wait_event(free)
+        with torch.cuda.stream(self.copy):
+            x.copy_(x_host, non_blocking=True)
+            t.copy_(t_host, non_blocking=True)
+            ready = torch.cuda.Event()
+            ready.record(self.copy)
+        return x, t, ready, slot
+
+    def done(self, slot: int, stream: torch.cuda.Stream) -> None:
+        """The step that reads `slot` is queued on `stream`: the set may be refilled once it has run."""
+        e = torch.cuda.Event()
+        e.record(stream)
+        self.sets[slot][2] = e
+
+
+def step_from_host(feed: HostFeed, x_host: torch.Tensor, t_host: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                   ws: MLPWorkspace, loss_host: torch.Tensor, stream: torch.cuda.Stream | None = None) -> None:
+    """One step whose batch and target come from host memory and whose loss goes back to it, all queued on `stream`
+    (torch's current stream by default) behind the feed's copies; returns at once."""
+    stream = torch.cuda.current_stream(w1.device) if stream is None else stream
+    x, t, ready, slot = feed.put(x_host, t_host)
+    stream.wait_event(ready)
+    mlp_step(x, w1, w2, t, ws, stream.cuda_stream)
+    with torch.cuda.stream(stream):
+        loss_host.copy_(ws.loss, non_blocking=True)
+    feed.done(slot, stream)
+
+
 def mlp_flops(batch: int, d_in: int, d_hidden: int, d_out: int) -> float:
     """Six products of 2 * batch * d_in * d_hidden (= 2 * batch * d_hidden * d_out when d_in = d_out) flops each."""
     return 2.0 * batch * d_hidden * (3 * d_in + 3 * d_out)

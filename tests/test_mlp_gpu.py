@@ -67,3 +67,34 @@ def test_autograd_backward_runs_the_library_and_matches_torch(cuda):
     assert abs(loss.item() - ref.item()) <= 1e-2 * ref.item()
     for got, want in ((xr.grad, X.grad), (w1.grad, W1.grad), (w2.grad, W2.grad)):
         assert _rel(got.float().cpu().numpy(), want.cpu().numpy()) < 2e-2
+
+
+def test_steps_fed_from_host_memory_match_steps_on_device_copies(cuda):
+    """mlp.step_from_host: batches copied in on the feed's stream while the step before computes, the loss copied
+    back; every step's loss and gradients equal, bit for bit, those of the same step run from device tensors."""
+    B, D, Hd, O = 512, 256, 1024, 512
+    g = torch.Generator(device=cuda).manual_seed(3)
+    w1 = (torch.randn(D, Hd, device=cuda, generator=g) * 0.02).bfloat16()
+    w2 = (torch.randn(Hd, O, device=cuda, generator=g) * 0.02).bfloat16()
+    batches = [(torch.randn(B, D, device=cuda, generator=g).bfloat16(), torch.randn(B, O, device=cuda, generator=g))
+               for _ in range(3)]
+    want = []
+    for x, t in batches:
+        ws = mlp.mlp_step(x, w1, w2, t)
+        want.append((ws.loss.clone(), ws.dw1.clone(), ws.dw2.clone(), ws.dx.clone()))
+    host = [(x.cpu().pin_memory(), t.cpu().pin_memory()) for x, t in batches]
+    feed = mlp.HostFeed(B, D, O, cuda)
+    ws = mlp.MLPWorkspace(B, D, Hd, O, cuda)
+    losses = [torch.empty(1, dtype=torch.float32).pin_memory() for _ in range(5)]
+    stream = torch.cuda.current_stream(cuda)
+    for i in range(5):
+        x_h, t_h = host[i % 3]
+        mlp.step_from_host(feed, x_h, t_h, w1, w2, ws, losses[i], stream)
+        if i == 4:
+            torch.cuda.synchronize()
+            w_loss, w_dw1, w_dw2, w_dx = want[i % 3]
+            assert torch.equal(ws.dw1, w_dw1) and torch.equal(ws.dw2, w_dw2) and torch.equal(ws.dx, w_dx)
+    torch.cuda.synchronize()
+    cairn_b200.stream_status()
+    for i in range(5):
+        assert losses[i].item() == want[i % 3][0].item(), i
