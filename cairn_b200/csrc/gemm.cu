@@ -710,17 +710,8 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       // for the pair's first segment, slot 1 for its last); the fix-up after the grid barrier adds the parts.
       const bool split = kb_begin > 0 || kb_end < num_kb;
       float* slot = p.ws + static_cast<std::size_t>(2 * (2 * pair + static_cast<int>(rank)) + (it ? 1 : 0)) * SLOT;
-#pragma unroll 1
-      for (int ci = 0; ci < CHUNKS; ++ci) {
-        const int c = col0 + ci * 32;
-        std::uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c, r);
-        tmem_wait_ld();
-        if (ci + 1 == CHUNKS) {  // this warp's part of the accumulator is in registers
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
-        }
+      // Writes chunk ci (in r) to its destination: the tile's columns, or this segment's workspace slot.
+      auto emit = [&](int ci, const std::uint32_t (&r)[32]) {
         if (split) {
           float4* dst = reinterpret_cast<float4*>(slot) + partial_cell(ew, ci, CHUNKS) + lane;
 #pragma unroll
@@ -728,8 +719,28 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
             __stcg(dst + q * 32, make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
                                              __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
         } else {
-          store_chunk_staged(p, row0, nb * S::TILE_N + c, r, stage, lane);
+          store_chunk_staged(p, row0, nb * S::TILE_N + col0 + ci * 32, r, stage, lane);
         }
+      };
+      // The drain is double-buffered: a TMEM load takes several hundred cycles to reach the registers, so each
+      // chunk's load is issued before the chunk ahead of it is written out. The accumulator goes back to the MMA
+      // issuer once the last chunk's load has landed. CHUNKS is even (8 for G = 2, 4 for G = 1).
+      std::uint32_t ra[32], rb[32];
+      tmem_ld_32x32b_x32(t_row + col0, ra);
+#pragma unroll 1
+      for (int ci = 0; ci < CHUNKS; ci += 2) {
+        tmem_wait_ld(ra);
+        tmem_ld_32x32b_x32(t_row + col0 + (ci + 1) * 32, rb);
+        emit(ci, ra);
+        tmem_wait_ld(rb);
+        if (ci + 2 < CHUNKS) {
+          tmem_ld_32x32b_x32(t_row + col0 + (ci + 2) * 32, ra);
+        } else {  // this warp's part of the accumulator is in registers
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+        }
+        emit(ci + 1, rb);
       }
     }
     if (p.streamk) {
