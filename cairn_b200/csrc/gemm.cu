@@ -53,6 +53,7 @@ struct TcParams {
   const float* bias;
   int act;
   const std::uint16_t* mask;  // OUT_BF16 only: keep an output where this m x n bf16 array is > 0, else 0
+  int mask_vec;               // mask starts on 16 bytes (its rows then do too whenever vec holds)
   int vec;        // every output row starts on 16 bytes and holds whole 16-byte groups
   std::uint32_t* fault;
   int streamk;            // split the tiles' k-blocks evenly over the pairs (pair kernel only)
@@ -346,7 +347,7 @@ constexpr int STAGE_PITCH = 80;                  // bytes per staged row: 64 of 
 constexpr int STAGE_BYTES = 32 * STAGE_PITCH;    // one warp's buffer
 
 __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int col, const std::uint32_t (&r)[32],
-                                                float (&v)[32]) {
+                                                float (&v)[32], bool apply_mask) {
   float bias[32];
   if (p.bias != nullptr && col + 32 <= p.n && (reinterpret_cast<std::uintptr_t>(p.bias + col) & 15u) == 0) {
     const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
@@ -368,7 +369,7 @@ __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int 
     if (p.act == ACT_RELU) x = x < 0.0f ? 0.0f : x;
     v[j] = x;
   }
-  if (p.mask != nullptr && row < p.m) {
+  if (apply_mask && p.mask != nullptr && row < p.m) {
     const std::uint16_t* mrow = p.mask + static_cast<std::size_t>(row) * p.n + col;
 #pragma unroll
     for (int j = 0; j < 32; ++j)
@@ -376,13 +377,29 @@ __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int 
   }
 }
 
+// The ReLU's backward on two packed bf16 outputs: each 16-bit half of `out2` stays where the matching half of
+// `mask2` (bf16 bits of the forward's output) is > 0 and becomes +0 elsewhere. A bf16 value is > 0 exactly when its
+// bits, read as an unsigned 16-bit number, lie in [0x0001, 0x7f80] (positive subnormals up to +inf; +0, every
+// negative value and NaN fall outside), so this is the same test as the float comparison, and zeroing after the
+// rounding gives the bits that rounding a zeroed value does.
+__device__ __forceinline__ std::uint32_t keep_where_positive(std::uint32_t out2, std::uint32_t mask2) {
+  std::uint32_t kept = 0;
+  if ((mask2 & 0xffffu) - 1u < 0x7f80u) kept |= out2 & 0xffffu;
+  if ((mask2 >> 16) - 1u < 0x7f80u) kept |= out2 & 0xffff0000u;
+  return kept;
+}
+
 // Stores the warp's 32 x 32 chunk whose first row is row0 (this thread holds row row0 + lane) at column col.
 __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, int col, const std::uint32_t (&r)[32],
                                                    std::uint8_t* stage, int lane) {
   const int seg = lane & 3, sub = lane >> 2;  // read-back: 4 threads per row (16 bytes each), 8 rows per pass
   if (p.out_kind == OUT_BF16) {
+    // With 16-byte rows the ReLU-gradient mask is read where each 16-byte group is written back: one coalesced
+    // 16-byte load per 8 outputs (8 rows x 64 bytes per instruction) instead of 32 two-byte loads per thread
+    // scattered over 32 rows.
+    const bool late_mask = p.mask != nullptr && p.vec && p.mask_vec;
     float v[32];
-    epilogue_values(p, row0 + lane, col, r, v);
+    epilogue_values(p, row0 + lane, col, r, v, !late_mask);
     uint4* mine = reinterpret_cast<uint4*>(stage + lane * STAGE_PITCH);
 #pragma unroll
     for (int q = 0; q < 4; ++q) {
@@ -401,10 +418,18 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
 #pragma unroll
     for (int pass = 0; pass < 4; ++pass) {
       const int rr = pass * 8 + sub, row = row0 + rr, c0 = col + seg * 8;
-      const uint4 w = *reinterpret_cast<const uint4*>(stage + rr * STAGE_PITCH + seg * 16);
+      uint4 w = *reinterpret_cast<const uint4*>(stage + rr * STAGE_PITCH + seg * 16);
       if (row < p.m) {
         __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + static_cast<std::size_t>(row) * p.n + c0;
         if (p.vec && c0 + 8 <= p.n) {
+          if (late_mask) {
+            const uint4 mk =
+                __ldg(reinterpret_cast<const uint4*>(p.mask + static_cast<std::size_t>(row) * p.n + c0));
+            w.x = keep_where_positive(w.x, mk.x);
+            w.y = keep_where_positive(w.y, mk.y);
+            w.z = keep_where_positive(w.z, mk.z);
+            w.w = keep_where_positive(w.w, mk.w);
+          }
           *reinterpret_cast<uint4*>(dst) = w;
         } else {
           const std::uint16_t* h = reinterpret_cast<const std::uint16_t*>(&w);
@@ -1192,6 +1217,7 @@ cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream, int sms, std::ui
   p.bias = g.bias;
   p.act = g.act;
   p.mask = g.mask;
+  p.mask_vec = g.mask != nullptr && aligned16(g.mask);
   p.fault = fault;
   const std::uint64_t out_es = g.out_kind == OUT_BF16 ? 2 : 4;
   p.vec = aligned16(g.out) && (g.n * out_es) % 16 == 0;

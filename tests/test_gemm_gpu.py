@@ -269,3 +269,39 @@ def test_baseline_config_1_f32_gemm_512_cubed(cuda):
     mag = np.abs(a.reshape(m, k)).astype(np.float64) @ np.abs(b.reshape(k, n)).astype(np.float64)
     tol = (2.0**-9 + (k + 1) * 2.0**-22) * mag
     assert (np.abs(ct.cpu().numpy().reshape(m, n) - want.reshape(m, n)) <= tol).all()
+
+
+# bf16 bit patterns of every kind a ReLU's forward output can hold: +-0, +-subnormal, +-normal, +-max, +-inf, NaNs
+MASK_SPECIALS = np.asarray([0x0000, 0x8000, 0x0001, 0x8001, 0x007F, 0x0080, 0x3F80, 0xBF80, 0x7F7F, 0xFF7F, 0x7F80,
+                            0xFF80, 0x7FC0, 0xFFC0, 0x7F81], np.uint16)
+
+
+@pytest.mark.parametrize("m,n,k,trans_b", [(512, 768, 128, True), (256, 1024, 256, False), (300, 260, 64, True),
+                                           (64, 200, 32, True)])
+def test_relu_grad_is_the_product_kept_where_the_forward_was_positive(cuda, m, n, k, trans_b):
+    """cairn_b200_gemm_relu_grad against the plain bf16 product of the same operands with the mask applied on the
+    host: the product's bits wherever the mask is > 0 (as a float), +0 elsewhere. The shapes reach the pair tile
+    with 16-byte rows (the mask read where the outputs are written back), rows off 16 bytes (n = 260, the mask read
+    per element) and the one-SM tile (m = 64)."""
+    rng = np.random.default_rng(m + n + k)
+    a = inputs.encode("bf16", rng.standard_normal(m * k))
+    b = inputs.encode("bf16", rng.standard_normal(k * n))
+    mask = np.where(rng.random(m * n) < 0.5, inputs.encode("bf16", rng.standard_normal(m * n)),
+                    rng.choice(MASK_SPECIALS, m * n)).astype(np.uint16)
+    at = to_dev("bf16", a, cuda).view(m, k)
+    bt = to_dev("bf16", b, cuda).view(n, k) if trans_b else to_dev("bf16", b, cuda).view(k, n)
+    mt = to_dev("bf16", mask, cuda)
+    plain = cairn_b200.gemm(at, bt, trans_b=trans_b, out_dtype=torch.bfloat16)
+    got = torch.empty(m, n, dtype=torch.bfloat16, device=cuda)
+    lib = cairn_b200.lib()
+    status = lib.cairn_b200_gemm_relu_grad(torch.cuda.current_stream(cuda).cuda_stream, cairn_b200._lib.BF16, m, n, k,
+                                           at.data_ptr(), 0, bt.data_ptr(), int(trans_b), got.data_ptr(),
+                                           mt.data_ptr())
+    assert status == 0
+    cairn_b200.stream_status()
+    positive = inputs.decode("bf16", mask) > 0
+    plain_bits = plain.view(torch.int16).cpu().numpy().view(np.uint16).ravel()
+    got_bits = got.view(torch.int16).cpu().numpy().view(np.uint16).ravel()
+    want = np.where(positive, plain_bits, np.uint16(0))
+    bad = np.flatnonzero(got_bits != want)
+    assert bad.size == 0, (bad[:4], got_bits[bad[:4]], want[bad[:4]], mask[bad[:4]])
