@@ -26,6 +26,7 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -346,6 +347,35 @@ __global__ void __launch_bounds__(192, 1)
 constexpr int STAGE_PITCH = 80;                  // bytes per staged row: 64 of data, 16 of padding
 constexpr int STAGE_BYTES = 32 * STAGE_PITCH;    // one warp's buffer
 
+// Asks L2 for the line-aligned span of row `row` of an m x n row-major array (es bytes an element) covering columns
+// [c_begin, c_end) that an epilogue warp will read while it drains: the ReLU-gradient mask, or the old C of the
+// accumulate form. Issued before the tile's accumulator is ready, so the drain (which the next tile's MMAs wait for
+// when the accumulator is single) finds those lines in L2 instead of waiting on DRAM. Every address stays inside the
+// array: the span starts at or after the row's first byte and ends before its column c_end.
+__device__ __forceinline__ void prefetch_row_span(const void* base, int es, const TcParams& p, int row, int c_begin,
+                                                  int c_end) {
+  if (row >= p.m) return;
+  const int end = c_end < p.n ? c_end : p.n;
+  if (c_begin >= end) return;
+  const char* first = static_cast<const char*>(base) + static_cast<std::size_t>(row) * p.n * es;
+  const std::size_t stop = static_cast<std::size_t>(end) * es;
+  for (std::size_t off = (static_cast<std::size_t>(c_begin) * es) & ~static_cast<std::size_t>(127); off < stop;
+       off += 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(first + off));
+}
+
+// The ReLU's backward on two packed bf16 outputs: each 16-bit half of `out2` stays where the matching half of
+// `mask2` (bf16 bits of the forward's output) is > 0 and becomes +0 elsewhere. A bf16 value is > 0 exactly when its
+// bits, read as an unsigned 16-bit number, lie in [0x0001, 0x7f80] (positive subnormals up to +inf; +0, every
+// negative value and NaN fall outside), so this is the same test as the float comparison, and zeroing after the
+// rounding gives the bits that rounding a zeroed value does.
+__device__ __forceinline__ std::uint32_t keep_where_positive(std::uint32_t out2, std::uint32_t mask2) {
+  std::uint32_t kept = 0;
+  if ((mask2 & 0xffffu) - 1u < 0x7f80u) kept |= out2 & 0xffffu;
+  if ((mask2 >> 16) - 1u < 0x7f80u) kept |= out2 & 0xffff0000u;
+  return kept;
+}
+
 __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int col, const std::uint32_t (&r)[32],
                                                 float (&v)[32], bool apply_mask) {
   float bias[32];
@@ -377,58 +407,107 @@ __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int 
   }
 }
 
-// The ReLU's backward on two packed bf16 outputs: each 16-bit half of `out2` stays where the matching half of
-// `mask2` (bf16 bits of the forward's output) is > 0 and becomes +0 elsewhere. A bf16 value is > 0 exactly when its
-// bits, read as an unsigned 16-bit number, lie in [0x0001, 0x7f80] (positive subnormals up to +inf; +0, every
-// negative value and NaN fall outside), so this is the same test as the float comparison, and zeroing after the
-// rounding gives the bits that rounding a zeroed value does.
-__device__ __forceinline__ std::uint32_t keep_where_positive(std::uint32_t out2, std::uint32_t mask2) {
-  std::uint32_t kept = 0;
-  if ((mask2 & 0xffffu) - 1u < 0x7f80u) kept |= out2 & 0xffffu;
-  if ((mask2 >> 16) - 1u < 0x7f80u) kept |= out2 & 0xffff0000u;
-  return kept;
-}
-
-// Stores the warp's 32 x 32 chunk whose first row is row0 (this thread holds row row0 + lane) at column col.
+// Stores the warp's 32 x 32 chunk whose first row is row0 (this thread holds row row0 + lane) at column col, through
+// the warp's staging rows, so each write-back pass moves 8 rows x 64 bytes.
+// LOADS = false, for epilogues that read no memory (the double-buffered drain): bias, ReLU and the mask (read per
+//   element, should one be given) over all 32 values at once, then bf16 packing; f32 goes through in two 16-column
+//   halves.
+// LOADS = true, for epilogues that read memory (the single-buffered drain, whose registers allow it): bf16 values are
+//   formed eight at a time (bias, ReLU, per-element mask) straight into the staging row, so few are live beside
+//   the chunk; with 16-byte rows the ReLU-gradient mask is instead read at write-back, one coalesced 16-byte load
+//   per 8 outputs, and the accumulate form's old values likewise, a half's four at once. Both kinds of load are
+//   issued together before the first store: a load after a store to the output could not be moved above it,
+//   which would serialise the passes on the load's latency.
+template <bool LOADS>
 __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, int col, const std::uint32_t (&r)[32],
                                                    std::uint8_t* stage, int lane) {
   const int seg = lane & 3, sub = lane >> 2;  // read-back: 4 threads per row (16 bytes each), 8 rows per pass
   if (p.out_kind == OUT_BF16) {
-    // With 16-byte rows the ReLU-gradient mask is read where each 16-byte group is written back: one coalesced
-    // 16-byte load per 8 outputs (8 rows x 64 bytes per instruction) instead of 32 two-byte loads per thread
-    // scattered over 32 rows.
-    const bool late_mask = p.mask != nullptr && p.vec && p.mask_vec;
-    float v[32];
-    epilogue_values(p, row0 + lane, col, r, v, !late_mask);
+    const bool late_mask = LOADS && p.mask != nullptr && p.vec && p.mask_vec;
     uint4* mine = reinterpret_cast<uint4*>(stage + lane * STAGE_PITCH);
+    if constexpr (!LOADS) {
+      float v[32];
+      epilogue_values(p, row0 + lane, col, r, v, true);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      uint4 w;
-      __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
-      __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
-      __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
-      __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
-      std::memcpy(&w.x, &h0, 4);
-      std::memcpy(&w.y, &h1, 4);
-      std::memcpy(&w.z, &h2, 4);
-      std::memcpy(&w.w, &h3, 4);
-      mine[q] = w;
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
+        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
+        __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
+        std::memcpy(&w.x, &h0, 4);
+        std::memcpy(&w.y, &h1, 4);
+        std::memcpy(&w.z, &h2, 4);
+        std::memcpy(&w.w, &h3, 4);
+        mine[q] = w;
+      }
+    } else {
+      const int row = row0 + lane;
+      const std::uint16_t* mrow = (!late_mask && p.mask != nullptr && row < p.m)
+                                      ? p.mask + static_cast<std::size_t>(row) * p.n + col
+                                      : nullptr;
+      const bool bias_vec =
+          p.bias != nullptr && col + 32 <= p.n && (reinterpret_cast<std::uintptr_t>(p.bias + col) & 15u) == 0;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float b[8];
+        if (bias_vec) {
+          const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + col) + 2 * q);
+          const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + col) + 2 * q + 1);
+          b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z, b[7] = b1.w;
+        } else {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const int c = col + 8 * q + j;
+            b[j] = (p.bias != nullptr && c < p.n) ? __ldg(p.bias + c) : 0.0f;
+          }
+        }
+        std::uint32_t packed[4];
+#pragma unroll
+        for (int j = 0; j < 8; j += 2) {
+          float x0 = __fadd_rn(__uint_as_float(r[8 * q + j]), b[j]);
+          float x1 = __fadd_rn(__uint_as_float(r[8 * q + j + 1]), b[j + 1]);
+          if (p.act == ACT_RELU) {
+            x0 = x0 < 0.0f ? 0.0f : x0;
+            x1 = x1 < 0.0f ? 0.0f : x1;
+          }
+          if (mrow != nullptr) {  // the ReLU's backward: the gradient passes where the forward's output was positive
+            const int c = col + 8 * q + j;
+            if (c < p.n && !(__uint_as_float(static_cast<std::uint32_t>(__ldg(mrow + 8 * q + j)) << 16) > 0.0f))
+              x0 = 0.0f;
+            if (c + 1 < p.n &&
+                !(__uint_as_float(static_cast<std::uint32_t>(__ldg(mrow + 8 * q + j + 1)) << 16) > 0.0f))
+              x1 = 0.0f;
+          }
+          const __nv_bfloat162 h = __floats2bfloat162_rn(x0, x1);
+          std::memcpy(&packed[j / 2], &h, 4);
+        }
+        mine[q] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      }
+    }
+    uint4 mk[4];
+    if (late_mask) {
+#pragma unroll
+      for (int pass = 0; pass < 4; ++pass) {
+        const int mr = row0 + pass * 8 + sub, c0 = col + seg * 8;
+        mk[pass] = (mr < p.m && c0 + 8 <= p.n)
+                       ? __ldg(reinterpret_cast<const uint4*>(p.mask + static_cast<std::size_t>(mr) * p.n + c0))
+                       : make_uint4(0u, 0u, 0u, 0u);
+      }
     }
     __syncwarp();
 #pragma unroll
     for (int pass = 0; pass < 4; ++pass) {
-      const int rr = pass * 8 + sub, row = row0 + rr, c0 = col + seg * 8;
+      const int rr = pass * 8 + sub, orow = row0 + rr, c0 = col + seg * 8;
       uint4 w = *reinterpret_cast<const uint4*>(stage + rr * STAGE_PITCH + seg * 16);
-      if (row < p.m) {
-        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + static_cast<std::size_t>(row) * p.n + c0;
+      if (orow < p.m) {
+        __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(p.out) + static_cast<std::size_t>(orow) * p.n + c0;
         if (p.vec && c0 + 8 <= p.n) {
           if (late_mask) {
-            const uint4 mk =
-                __ldg(reinterpret_cast<const uint4*>(p.mask + static_cast<std::size_t>(row) * p.n + c0));
-            w.x = keep_where_positive(w.x, mk.x);
-            w.y = keep_where_positive(w.y, mk.y);
-            w.z = keep_where_positive(w.z, mk.z);
-            w.w = keep_where_positive(w.w, mk.w);
+            w.x = keep_where_positive(w.x, mk[pass].x);
+            w.y = keep_where_positive(w.y, mk[pass].y);
+            w.z = keep_where_positive(w.z, mk[pass].z);
+            w.w = keep_where_positive(w.w, mk[pass].w);
           }
           *reinterpret_cast<uint4*>(dst) = w;
         } else {
@@ -442,6 +521,7 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
     __syncwarp();
   } else {
     const bool acc = p.out_kind == OUT_ACC_F32;
+    const bool batch_old = LOADS && acc && p.vec;
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       float4* mine = reinterpret_cast<float4*>(stage + lane * STAGE_PITCH);
@@ -449,20 +529,31 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
       for (int q = 0; q < 4; ++q)
         mine[q] = make_float4(__uint_as_float(r[16 * half + 4 * q]), __uint_as_float(r[16 * half + 4 * q + 1]),
                               __uint_as_float(r[16 * half + 4 * q + 2]), __uint_as_float(r[16 * half + 4 * q + 3]));
+      float4 old[4];
+      if (batch_old) {
+#pragma unroll
+        for (int pass = 0; pass < 4; ++pass) {
+          const int orow = row0 + pass * 8 + sub, c0 = col + 16 * half + seg * 4;
+          old[pass] = (orow < p.m && c0 + 4 <= p.n)
+                          ? *reinterpret_cast<const float4*>(static_cast<const float*>(p.out) +
+                                                             static_cast<std::size_t>(orow) * p.n + c0)
+                          : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+      }
       __syncwarp();
 #pragma unroll
       for (int pass = 0; pass < 4; ++pass) {
-        const int rr = pass * 8 + sub, row = row0 + rr, c0 = col + 16 * half + seg * 4;
+        const int rr = pass * 8 + sub, orow = row0 + rr, c0 = col + 16 * half + seg * 4;
         float4 w = *reinterpret_cast<const float4*>(stage + rr * STAGE_PITCH + seg * 16);
-        if (row < p.m) {
-          float* dst = static_cast<float*>(p.out) + static_cast<std::size_t>(row) * p.n + c0;
+        if (orow < p.m) {
+          float* dst = static_cast<float*>(p.out) + static_cast<std::size_t>(orow) * p.n + c0;
           if (p.vec && c0 + 4 <= p.n) {
             if (acc) {
-              const float4 old = *reinterpret_cast<const float4*>(dst);
-              w.x = __fadd_rn(old.x, w.x);
-              w.y = __fadd_rn(old.y, w.y);
-              w.z = __fadd_rn(old.z, w.z);
-              w.w = __fadd_rn(old.w, w.w);
+              const float4 o = batch_old ? old[pass] : *reinterpret_cast<const float4*>(dst);
+              w.x = __fadd_rn(o.x, w.x);
+              w.y = __fadd_rn(o.y, w.y);
+              w.z = __fadd_rn(o.z, w.z);
+              w.w = __fadd_rn(o.w, w.w);
             }
             *reinterpret_cast<float4*>(dst) = w;
           } else {
@@ -555,7 +646,7 @@ template <int G> struct PairShape {
   static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_HALF) + 256 + EPI_WARPS * STAGE_BYTES;
 };
 
-template <int FMT, int G>
+template <int FMT, int G, bool READS>
 __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const TcParams p) {
@@ -725,11 +816,18 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
     for (; work.next(t, kb_begin, kb_end); ++it) {
       const std::uint32_t acc = S::ACCS == 2 ? (it & 1u) : 0u;
       const std::uint32_t acc_phase = S::ACCS == 2 ? ((it >> 1) & 1u) : (it & 1u);
-      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.fault, FAULT_WAIT_TFULL)) break;
-      tc_fence_after();
       int mb, nb;
       tile_of(t, num_m, num_n, mb, nb);
       const int row0 = mb * 2 * HALF + static_cast<int>(rank) * HALF + quarter * 32;
+      const int c_first = nb * S::TILE_N + col0;  // this warp's first output column of the tile
+      if constexpr (READS) {
+        if (p.mask != nullptr)
+          prefetch_row_span(p.mask, 2, p, row0 + lane, c_first, c_first + COLS_PER_WARP);
+        else if (p.out_kind == OUT_ACC_F32 && kb_begin == 0 && kb_end == num_kb)
+          prefetch_row_span(p.out, 4, p, row0 + lane, c_first, c_first + COLS_PER_WARP);
+      }
+      if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.fault, FAULT_WAIT_TFULL)) break;
+      tc_fence_after();
       const std::uint32_t t_row = tmem_base + (static_cast<std::uint32_t>(quarter * 32) << 16) + acc * PAIR_BN;
       // A segment holding part of a tile's k-blocks leaves its raw f32 sum in one of this CTA's two slots (slot 0
       // for the pair's first segment, slot 1 for its last); the fix-up after the grid barrier adds the parts.
@@ -744,28 +842,45 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
             __stcg(dst + q * 32, make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
                                              __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
         } else {
-          store_chunk_staged(p, row0, nb * S::TILE_N + col0 + ci * 32, r, stage, lane);
+          store_chunk_staged<READS>(p, row0, nb * S::TILE_N + col0 + ci * 32, r, stage, lane);
         }
       };
-      // The drain is double-buffered: a TMEM load takes several hundred cycles to reach the registers, so each
-      // chunk's load is issued before the chunk ahead of it is written out. The accumulator goes back to the MMA
-      // issuer once the last chunk's load has landed. CHUNKS is even (8 for G = 2, 4 for G = 1).
-      std::uint32_t ra[32], rb[32];
-      tmem_ld_32x32b_x32(t_row + col0, ra);
+      if constexpr (READS) {
+        // An epilogue that reads memory (the ReLU-gradient mask, or the old outputs of the accumulate form) keeps
+        // those loads in flight rather than the TMEM loads: single-buffered, so its registers hold a chunk's loads.
 #pragma unroll 1
-      for (int ci = 0; ci < CHUNKS; ci += 2) {
-        tmem_wait_ld(ra);
-        tmem_ld_32x32b_x32(t_row + col0 + (ci + 1) * 32, rb);
-        emit(ci, ra);
-        tmem_wait_ld(rb);
-        if (ci + 2 < CHUNKS) {
-          tmem_ld_32x32b_x32(t_row + col0 + (ci + 2) * 32, ra);
-        } else {  // this warp's part of the accumulator is in registers
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+        for (int ci = 0; ci < CHUNKS; ++ci) {
+          std::uint32_t r[32];
+          tmem_ld_32x32b_x32(t_row + col0 + ci * 32, r);
+          tmem_wait_ld(r);
+          if (ci + 1 == CHUNKS) {  // this warp's part of the accumulator is in registers
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+          }
+          emit(ci, r);
         }
-        emit(ci + 1, rb);
+      } else {
+        // Otherwise the drain is double-buffered: a TMEM load takes several hundred cycles to reach the registers,
+        // so each chunk's load is issued before the chunk ahead of it is written out. The accumulator goes back to
+        // the MMA issuer once the last chunk's load has landed. CHUNKS is even (8 for G = 2, 4 for G = 1).
+        std::uint32_t ra[32], rb[32];
+        tmem_ld_32x32b_x32(t_row + col0, ra);
+#pragma unroll 1
+        for (int ci = 0; ci < CHUNKS; ci += 2) {
+          tmem_wait_ld(ra);
+          tmem_ld_32x32b_x32(t_row + col0 + (ci + 1) * 32, rb);
+          emit(ci, ra);
+          tmem_wait_ld(rb);
+          if (ci + 2 < CHUNKS) {
+            tmem_ld_32x32b_x32(t_row + col0 + (ci + 2) * 32, ra);
+          } else {  // this warp's part of the accumulator is in registers
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
+          }
+          emit(ci + 1, rb);
+        }
       }
     }
     if (p.streamk) {
@@ -832,7 +947,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
         int mb, nb;
         tile_of(tt, num_m, num_n, mb, nb);
         const int w_quarter = (w + 2) & 3;  // epilogue warp w is warp w + 2: its TMEM lane quarter
-        store_chunk_staged(p, mb * 2 * HALF + rr * HALF + w_quarter * 32,
+        store_chunk_staged<READS>(p, mb * 2 * HALF + rr * HALF + w_quarter * 32,
                            nb * S::TILE_N + (w / 4) * COLS_PER_WARP + ci * 32, r, stage, lane);
       }
     }
@@ -1068,14 +1183,14 @@ cudaError_t launch_tc(const GemmArgs& g, const TcParams& p, cudaStream_t stream,
 }
 
 // The pair kernel's dynamic shared memory, set once per device and instantiation before its first launch.
-template <int FMT, int G> cudaError_t configure_pair() {
+template <int FMT, int G, bool READS> cudaError_t configure_pair() {
   static std::atomic<std::uint64_t> configured{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const std::uint64_t bit = 1ull << (dev & 63);
   if (configured.load(std::memory_order_acquire) & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(tc_gemm_pair_kernel<FMT, G>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  e = cudaFuncSetAttribute(tc_gemm_pair_kernel<FMT, G, READS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            PairShape<G>::SMEM);
   if (e != cudaSuccess) return e;
   configured.fetch_or(bit, std::memory_order_acq_rel);
@@ -1092,7 +1207,7 @@ template <int G> int resident_pairs(int sms) {
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   const int known = cached[dev & 63].load(std::memory_order_acquire);
   if (known) return known;
-  if (configure_pair<FMT_BF16, G>() != cudaSuccess) return 0;
+  if (configure_pair<FMT_BF16, G, false>() != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(sms, 1, 1);
   cfg.blockDim = dim3(PairShape<G>::THREADS, 1, 1);
@@ -1105,7 +1220,7 @@ template <int G> int resident_pairs(int sms) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_pair_kernel<FMT_BF16, G>, &cfg) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_pair_kernel<FMT_BF16, G, false>, &cfg) != cudaSuccess ||
       clusters <= 0) {
     cudaGetLastError();  // leave no sticky error behind for the launch to report
     return 0;
@@ -1127,7 +1242,10 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   const bool ok_b = g.trans_b ? encode(&tb, FMT, g.b, g.k, g.n, es, CH, HALF, false)
                               : encode(&tb, FMT, g.b, g.n, g.k, es, CH, CH, true);
   if (!ok_a || !ok_b) return cudaErrorInvalidValue;
-  cudaError_t e = configure_pair<FMT, G>();
+  // Epilogues that read memory (the ReLU-gradient mask, the accumulate form's old outputs) run their own
+  // instantiation, whose drain keeps those loads in flight; the others keep the double-buffered TMEM drain.
+  const bool reads = p.mask != nullptr || p.out_kind == OUT_ACC_F32;
+  cudaError_t e = reads ? configure_pair<FMT, G, true>() : configure_pair<FMT, G, false>();
   if (e != cudaSuccess) return e;
   const int tiles = ((p.m + 2 * HALF - 1) / (2 * HALF)) * ((p.n + S::TILE_N - 1) / S::TILE_N);
   const int num_kb = (p.k + CH - 1) / CH;
@@ -1151,7 +1269,8 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G>, ta, tb, q);
+  e = reads ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, true>, ta, tb, q)
+            : cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, false>, ta, tb, q);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }
