@@ -235,6 +235,10 @@ __device__ inline Part<T> fold_range_warp(In in, std::size_t begin, std::size_t 
 // 256-byte read a step). Measured on a B200 at n = 2^30: 4 or 8 per lane read more lines per step at the frontier
 // every look-back warp is reading, and ran slower.
 constexpr unsigned LOOK_PER_LANE = 1;
+// How long a looking-back lane sleeps between reads of a predecessor that has published nothing. Measured on a B200
+// at n = 2^30 (u32 add_wrap, the kernel alone): 32 ns doubling to 128 ran 3973 GB/s, a fixed 512 ns 4375, 32 doubling
+// to 1024 4293, to 2048 3796; starting the look-back only once the tile is loaded (3496) or raked (3415) was slower.
+constexpr unsigned LOOK_PAUSE_NS = 512;
 
 // Warp 0's look-back for tile t > 0: op over every element before the tile, in lane 0.
 template<class T, class In, class Fold>
@@ -258,12 +262,11 @@ __device__ inline Part<T> look_back(In in, std::size_t t, std::size_t tile_elems
 #pragma unroll
     for(int k = 0; k < K; ++k) {
       const long long pred = end - K * static_cast<long long>(lane) - k;
-      unsigned pause = 32;  // ns; doubled up to 128 so waiting lanes neither crowd the lines being published nor
-                            // sleep long past the moment a predecessor publishes (the workers wait on this warp)
+      // A lane whose predecessor has published nothing yet reads it again every LOOK_PAUSE_NS: about 444 blocks
+      // (three per SM) look back at once, and polls any faster crowd L2 with reads of the lines being published.
       while(pred >= 0 && f[k] == 0) {
         if(globaltimer() - start > wait_ns) break;
-        __nanosleep(pause);
-        pause = pause < 128 ? 2 * pause : pause;
+        __nanosleep(LOOK_PAUSE_NS);
         f[k] = st.read(static_cast<std::size_t>(pred), v[k]);
       }
       missing = missing || f[k] == 0;
