@@ -13,6 +13,7 @@
 //   - f32 terms are added in f64, which holds every f32 term exactly; the total is rounded to f32 once.
 //   - u64 terms carry cr::Sum's sticky overflow flag (runtime/cairn_runtime.hpp:158-166) through every fold.
 #include <cstdint>
+#include <cstring>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include "gemm.h"
@@ -285,17 +286,62 @@ __device__ __forceinline__ double block_sum_f64(double v, double* shared) {
   return t;
 }
 
+__device__ __forceinline__ std::uint32_t bf16x2_bits(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);  // lo at the lower address
+  std::uint32_t u;
+  std::memcpy(&u, &h, 4);
+  return u;
+}
+
+// VEC: y and t start on 16 bytes and dy on 8, so four elements move per float4 load and 8-byte store, UNROLL vectors
+// of each operand in flight per thread (the saxpy kernel's shape); the last n % 4 elements run in block 0.
+template <bool VEC>
 __global__ void __launch_bounds__(T, 2) mse_grad_kernel(std::size_t n, const float* y, const float* t,
                                                        __nv_bfloat16* dy, float scale, float* loss,
                                                        Partial* partials, unsigned int* ticket) {
   __shared__ double shared[WARPS];
   __shared__ bool last;
   const std::size_t stride = static_cast<std::size_t>(gridDim.x) * T;
-  double acc = 0.0;
-  for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x; i < n; i += stride) {
-    const float d = __fsub_rn(__ldcs(y + i), __ldcs(t + i));
-    dy[i] = __float2bfloat16_rn(__fmul_rn(d, scale));
-    acc += static_cast<double>(d) * static_cast<double>(d);  // exact: a product of two f32 fits a double
+  double acc = 0.0;  // each term d^2 is exact in f64: a product of two f32
+  std::size_t i = static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x;
+  if constexpr (VEC) {
+    const std::size_t n4 = n / 4;
+    const float4* y4 = reinterpret_cast<const float4*>(y);
+    const float4* t4 = reinterpret_cast<const float4*>(t);
+    uint2* d4 = reinterpret_cast<uint2*>(dy);
+    auto one = [&](std::size_t v, const float4& yv, const float4& tv) {
+      const float d0 = __fsub_rn(yv.x, tv.x), d1 = __fsub_rn(yv.y, tv.y), d2 = __fsub_rn(yv.z, tv.z),
+                  d3 = __fsub_rn(yv.w, tv.w);
+      __stcs(d4 + v, make_uint2(bf16x2_bits(__fmul_rn(d0, scale), __fmul_rn(d1, scale)),
+                                bf16x2_bits(__fmul_rn(d2, scale), __fmul_rn(d3, scale))));
+      acc += static_cast<double>(d0) * static_cast<double>(d0);
+      acc += static_cast<double>(d1) * static_cast<double>(d1);
+      acc += static_cast<double>(d2) * static_cast<double>(d2);
+      acc += static_cast<double>(d3) * static_cast<double>(d3);
+    };
+    for (; i + (UNROLL - 1) * stride < n4; i += UNROLL * stride) {
+      float4 yv[UNROLL], tv[UNROLL];
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) {
+        yv[u] = __ldcs(y4 + i + u * stride);
+        tv[u] = __ldcs(t4 + i + u * stride);
+      }
+#pragma unroll
+      for (int u = 0; u < UNROLL; ++u) one(i + u * stride, yv[u], tv[u]);
+    }
+    for (; i < n4; i += stride) one(i, __ldcs(y4 + i), __ldcs(t4 + i));
+    if (blockIdx.x == 0 && threadIdx.x < n - n4 * 4) {
+      const std::size_t j = n4 * 4 + threadIdx.x;
+      const float d = __fsub_rn(y[j], t[j]);
+      dy[j] = __float2bfloat16_rn(__fmul_rn(d, scale));
+      acc += static_cast<double>(d) * static_cast<double>(d);
+    }
+  } else {
+    for (; i < n; i += stride) {
+      const float d = __fsub_rn(__ldcs(y + i), __ldcs(t + i));
+      dy[i] = __float2bfloat16_rn(__fmul_rn(d, scale));
+      acc += static_cast<double>(d) * static_cast<double>(d);
+    }
   }
   const double s = block_sum_f64(acc, shared);
   if (threadIdx.x == 0) {
@@ -448,7 +494,11 @@ cudaError_t mse_grad_launch(std::size_t n, const float* y, const float* t, std::
   const int grid = stream_grid(sms);
   Partial* partials = static_cast<Partial*>(scratch);
   unsigned int* ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(scratch) + static_cast<std::size_t>(grid) * 32);
-  mse_grad_kernel<<<grid, T, 0, s>>>(n, y, t, reinterpret_cast<__nv_bfloat16*>(dy), scale, loss, partials, ticket);
+  auto* d = reinterpret_cast<__nv_bfloat16*>(dy);
+  if (aligned16(y) && aligned16(t) && (reinterpret_cast<std::uintptr_t>(dy) & 7u) == 0)
+    mse_grad_kernel<true><<<grid, T, 0, s>>>(n, y, t, d, scale, loss, partials, ticket);
+  else
+    mse_grad_kernel<false><<<grid, T, 0, s>>>(n, y, t, d, scale, loss, partials, ticket);
   return cudaGetLastError();
 }
 

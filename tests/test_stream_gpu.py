@@ -135,3 +135,30 @@ def test_baseline_2_30_saxpy_and_sums(cuda):
     del x
     u = torch.arange(n, device=cuda, dtype=torch.int64).view(torch.uint64)
     assert cairn_b200.reduce_sum(u) == n * (n - 1) // 2
+
+
+@pytest.mark.parametrize("n", [0, 3, 4, 1_000_003, (1 << 22) + 5])
+@pytest.mark.parametrize("offset", [0, 1])
+def test_mse_gradient_bit_for_bit_and_its_loss(cuda, n, offset):
+    """cairn_b200_mse_grad (the MLP step's head): dy[i] = bf16((y[i] - t[i]) * (2 / n)), each operation rounded once
+    as the oracle's step does it, bit for bit; loss = f32(sum (y - t)^2 / n) with the sum in f64, within one f32
+    ulp of numpy's (the two add the exact squares in different orders). Offset 1 leaves the views off 16 bytes (the
+    per-element path); n = 1,000,003 and 2^22 + 5 reach the vector path's tail."""
+    rng = np.random.default_rng(n + offset)
+    y_np = rng.standard_normal(n + offset).astype(np.float32)
+    t_np = rng.standard_normal(n + offset).astype(np.float32)
+    y = torch.from_numpy(y_np).to(cuda)[offset:]
+    t = torch.from_numpy(t_np).to(cuda)[offset:]
+    dy = torch.empty(n + offset, dtype=torch.int16, device=cuda)[offset:]
+    loss = torch.full((1,), float("nan"), dtype=torch.float32, device=cuda)
+    lib = cairn_b200.lib()
+    stream = torch.cuda.current_stream(cuda).cuda_stream
+    assert lib.cairn_b200_mse_grad(stream, n, y.data_ptr(), t.data_ptr(), dy.data_ptr(), loss.data_ptr()) == 0
+    cairn_b200.stream_status()
+    d = y_np[offset:] - t_np[offset:]  # f32 subtraction, rounded once
+    scale = np.float32(2.0) / np.float32(n) if n else np.float32(0.0)
+    want_dy = inputs.encode("bf16", (d * scale).astype(np.float32))
+    assert np.array_equal(dy.cpu().numpy().view(np.uint16), want_dy)
+    want_loss = np.float32(np.sum(d.astype(np.float64) ** 2) / n) if n else np.float32(0.0)
+    got = np.float32(loss.item())
+    assert abs(int(got.view(np.int32)) - int(want_loss.view(np.int32))) <= 1, (got, want_loss)
