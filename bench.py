@@ -554,6 +554,105 @@ def cpu_mlp_sample(budget_s: float):
 
 
 # ---------------------------------------------------------------------------------------------------------------------
+REF_DEVICE = ROOT / "baseline" / "_ref" / "libemitted_ref.so"
+
+
+def reference_device_measure(args) -> dict:
+    """The reference's own CUDA path on this GPU (baseline/_ref/libemitted_ref.so: tests/dropin/emitted_program.cu
+    built over the reference's runtime headers alone, for sm_100a): its WMMA multiply (cr::tensor::launch, 64 x 64
+    tiles), its lane kernel (cr::gpu::run), its CUB collectors (reduce_on) and its scan_into over CUB. Runs in a
+    process of its own, after this project's timed region; inputs are resident in HBM. Enqueued entries (cq_) are
+    timed with CUDA events on the stream they are given; the cf_ sums, which return their total to the host, by the
+    host clock around the call (each includes the total's copy back and the wait, as the reference's entry does)."""
+    import torch
+
+    h = C.CDLL(str(REF_DEVICE))
+    z, p = C.c_size_t, C.c_void_p
+    sig = {"cq_gemm": (None, [p, z, z, z, z, p, z, p, z, p]), "cq_saxpy": (None, [p, z, p, p, p, C.c_float]),
+           "cf_dsum": (C.c_float, [z, p]), "cf_usum": (C.c_uint64, [z, p]), "cq_wscan": (None, [p, z, p, p])}
+    for name, (res, argt) in sig.items():
+        f = getattr(h, name)
+        f.restype, f.argtypes = res, argt
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    g = torch.Generator(device=dev).manual_seed(0)
+    w = args.workload
+
+    def events(fn, steps: int, warmup: int) -> float:
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / steps
+
+    def clock(fn, steps: int, warmup: int) -> float:
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(steps):
+            fn()
+        return (time.perf_counter() - t0) * 1e3 / steps
+
+    if w in ("gemm", "gemm5"):
+        m, n, k = (4096, 4096, 4096) if w == "gemm" else (65536, 8192, 8192)
+        a = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+        b = (torch.randn(k, n, device=dev, generator=g) * (1.0 if w == "gemm" else 0.02)).to(torch.bfloat16)
+        c = torch.zeros(m, n, device=dev)
+        ms = events(lambda: h.cq_gemm(stream.cuda_stream, m, n, k, m * n, c.data_ptr(), m * k, a.data_ptr(), k * n,
+                                      b.data_ptr()), 3 if w == "gemm5" else 10, 1)
+        return {"value": 2.0 * m * n * k / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
+                "what": "the reference's mma_unordered (cr::tensor::launch: WMMA 16x16x16, 64 x 64 tiles) on "
+                        f"{m}x{n}x{k} bf16 with f32 C += A B (it has no fused bias/ReLU epilogue)"}
+    if w == "mlp":
+        return {"unavailable": "the reference's derive-grad backward runs on the host only, and its device multiply "
+                               "takes no transposed operand"}
+    n = 1 << args.log2n
+    if w == "saxpy":
+        x = torch.rand(n, device=dev, generator=g) * 2 - 1
+        y = torch.rand(n, device=dev, generator=g) * 2 - 1
+        out = torch.empty_like(x)
+        ms = events(lambda: h.cq_saxpy(stream.cuda_stream, n, out.data_ptr(), x.data_ptr(), y.data_ptr(), 2.5), 10, 2)
+        what, per = "cr::gpu::run of out[i] = a x[i] + y[i] (the reference's lane kernel)", 12
+    elif w == "sum_f32":
+        x = torch.rand(n, device=dev, generator=g) * 2 - 1
+        ms = clock(lambda: h.cf_dsum(n, x.data_ptr()), 10, 2)
+        what, per = "reduce_on<float> over CUB's DeviceReduce (total copied back and awaited)", 4
+    elif w == "sum_u64":
+        u = torch.arange(n, device=dev, dtype=torch.int64)
+        ms = clock(lambda: h.cf_usum(n, u.data_ptr()), 10, 2)
+        what, per = "reduce_on<Sum<u64>> over CUB's DeviceReduce (total copied back and awaited)", 8
+    else:  # scan
+        x = torch.randint(-2**31, 2**31 - 1, (n,), device=dev, dtype=torch.int32, generator=g)
+        out = torch.empty_like(x)
+        ms = events(lambda: h.cq_wscan(stream.cuda_stream, n, out.data_ptr(), x.data_ptr()), 10, 2)
+        what, per = "scan_into over CUB's DeviceScan (the reference context's scan, then its copy pass)", 8
+    return {"value": n * per / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms": ms, "what": what}
+
+
+def reference_device_leg(args) -> dict | None:
+    """Runs reference_device_measure in a fresh process (python bench.py --reference-device ...) and returns its
+    result, or a note saying why there is none."""
+    if not REF_DEVICE.exists():
+        return {"unavailable": "baseline/_ref/libemitted_ref.so is not built (it needs the CAIRN reference's headers)"}
+    cmd = [sys.executable, str(Path(__file__).resolve()), "--reference-device", "--workload", args.workload,
+           "--log2n", str(args.log2n)]
+    try:
+        done = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": "the reference's device path did not finish within 600 s"}
+    lines = [ln for ln in done.stdout.splitlines() if ln.startswith("{")]
+    if done.returncode != 0 or not lines:
+        return {"unavailable": f"the reference's device path exited {done.returncode}: {done.stderr[-300:]}"}
+    return json.loads(lines[-1])
+
+
 def reference_arm(args, dist: Dist) -> None:
     """The reference's own CPU implementation of the path (the CAIRN runtime's host code, oracle/_ref) on this box's
     host cores, rank 0 only, each step a bounded sample of the workload."""
@@ -626,7 +725,13 @@ def main() -> None:
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--log2n", type=int, default=30, help="saxpy/sum size 2^log2n (BASELINE: 30; smaller for ncu)")
+    ap.add_argument("--no-reference-device", action="store_true",
+                    help="skip the reference-on-B200 leg (the reference's own CUDA path, timed in a subprocess)")
+    ap.add_argument("--reference-device", action="store_true", help=argparse.SUPPRESS)  # that subprocess
     args = ap.parse_args()
+    if args.reference_device:
+        print(json.dumps(reference_device_measure(args)), flush=True)
+        return
     defaults = {"gemm": (2000, 50), "gemm5": (50, 5), "mlp": (40, 5), "saxpy": (100, 5), "sum_f32": (200, 5),
                 "sum_u64": (100, 5), "scan": (50, 5)}
     d_steps, d_warm = defaults[args.workload] if args.impl == "ours" else (5, 1)
@@ -700,6 +805,10 @@ def main() -> None:
             v, cores, kind, sample = cpu_stream_sample(args.workload, 12.0)
         cpu = {"value": v, "unit": unit, "cores": cores, "kind": kind, "sample": sample}
 
+    refdev = None
+    if dist.rank == 0 and dist.world == 1 and not args.no_reference_device:
+        refdev = reference_device_leg(args)
+
     launches = args.steps * (7 if isinstance(wl, Mlp) else 2 if isinstance(wl, Scan) else
                              1 if isinstance(wl, Gemm) or args.workload != "sum_f32" or dist.world == 1 else 2)
     line = {
@@ -714,6 +823,7 @@ def main() -> None:
                      "peak_source": f"{peak_source} ({'hbm_gbs' if bound == 'hbm' else ('bf16_tflops_sustained: a long step' if isinstance(wl, Mlp) or args.workload == 'gemm5' else 'bf16_tflops burst')})",
                      "traffic": traffic},
         "cpu_baseline": cpu,
+        "reference_on_b200": refdev,
         "clocks": clocks,
         "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,

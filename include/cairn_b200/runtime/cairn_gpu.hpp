@@ -8,6 +8,8 @@
 // directory's cairn_kernels.hpp (persistent, device-sized grids). Its `reduce` is this project's own kernel instead
 // of CUB's, and so are its scans (defined in this directory's cairn_cub.hpp).
 #pragma once
+// Marks a program built over these headers (the B200 machine) rather than over the reference's own.
+#define CAIRN_B200_MACHINE 1
 #if !defined(CAIRN_EMULATE)
 #include <cstdio>
 #include <cstring>

@@ -3,7 +3,9 @@
 // compiler/device/tensor.py:69-82 for the bodies): every function's body calls only the runtime's templates,
 // cr::gpu::run, cr::gpu::run_vector, cr::gpu::run_staged, cr::gpu::reduce_on, cr::gpu::scan_on, cr::gpu::compact_on and cr::tensor::launch. It is built against the CAIRN
 // runtime headers with include/cairn_b200/runtime ahead of them on the include path (tests/dropin/build_emitted.py),
-// so the same source runs on the B200 machine and libcairn_b200.so. Test input of tests/test_dropin_gpu.py.
+// so the same source runs on the B200 machine and libcairn_b200.so. Test input of tests/test_dropin_gpu.py. Built
+// over the reference's headers alone, the same source runs the reference's own CUDA machine (its lane kernels, CUB
+// collectors and WMMA multiply): the reference-on-B200 baseline bench.py times beside this project's kernels.
 #include <cstddef>
 #include <cstdint>
 #include "cairn_runtime.hpp"
@@ -124,10 +126,12 @@ void ci_blur(std::size_t n, float* out, const float* x) {
       },
       [](std::size_t cr_w) { return cr::gpu::tile_bytes<float>(cr_w); }, 128);
 }
+#if defined(CAIRN_B200_MACHINE)
 struct WrapAdd {
   CR_DEVICE std::uint32_t operator()(std::uint32_t p, std::uint32_t q) const { return cr::add_wrap(p, q); }
 };
 inline const std::uint32_t* x_none() { return nullptr; }
+#endif
 }  // namespace
 
 extern "C" {
@@ -173,6 +177,18 @@ void cf_gemm(std::size_t m, std::size_t n, std::size_t k, std::size_t cn, float*
   cr::disjoint(c, cn, B, bn);
   ci_gemm(m, n, k, c, cn, A, an, B, bn);
 }
+void cq_gemm(void* stream, std::size_t m, std::size_t n, std::size_t k, std::size_t cn, float* c, std::size_t an,
+             const std::uint16_t* a, std::size_t bn, const std::uint16_t* b) noexcept {
+  const auto* A = reinterpret_cast<const cr::bf16*>(a);
+  const auto* B = reinterpret_cast<const cr::bf16*>(b);
+  cr::view(c, cn);
+  cr::view(A, an);
+  cr::view(B, bn);
+  cr::disjoint(c, cn, A, an);
+  cr::disjoint(c, cn, B, bn);
+  cr::gpu::Enqueued queued(stream);
+  ci_gemm(m, n, k, c, cn, A, an, B, bn);
+}
 std::uint64_t cf_prefix(std::size_t n, std::uint64_t* out, const std::uint64_t* x) noexcept {
   cr::view(out, n);
   cr::view(x, n);
@@ -198,6 +214,7 @@ std::size_t cf_positives(std::size_t n, float* out, const float* x) noexcept {
   cr::view(x, n);
   return ci_positives(n, out, x);
 }
+#if defined(CAIRN_B200_MACHINE)  // entries of the B200 machine's own scan (absent from the reference's machine)
 // Not a cairnc entry: the machine's inclusive u64 scan with a zero wait for predecessors, so that blocks which find
 // a predecessor unpublished take the look-back's escape (folding the inputs before their tile themselves).
 void cf_prefix_escape(std::size_t n, std::uint64_t* out, const std::uint64_t* x) noexcept {
@@ -209,6 +226,7 @@ void cf_prefix_escape(std::size_t n, std::uint64_t* out, const std::uint64_t* x)
   cr::gpu::check(cudaStreamSynchronize(nullptr));
   cr::gpu::check(cudaFree(temp));
 }
+#endif
 void cf_blur(std::size_t n, float* out, const float* x) noexcept {
   cr::view(out, n);
   cr::view(x, n);
@@ -224,6 +242,7 @@ void cq_wscan(void* stream, std::size_t n, std::uint32_t* out, const std::uint32
       cr::gpu::here(), out, n, 0u, [] CR_DEVICE(std::uint32_t p, std::uint32_t q) { return cr::add_wrap(p, q); },
       [=] CR_DEVICE(std::size_t i) { return x[i]; });
 }
+#if defined(CAIRN_B200_MACHINE)
 // Not cairnc entries: the machine's inclusive u32 add_wrap scan kernel alone, on the caller's stream and scratch
 // (b200_scan_u32_scratch bytes), so a bench can time the kernel without the context's copy pass.
 std::size_t b200_scan_u32_scratch(std::size_t n) noexcept {
@@ -236,4 +255,5 @@ void b200_scan_u32(void* stream, std::size_t n, std::uint32_t* out, const std::u
   std::size_t bytes = b200_scan_u32_scratch(n);
   cr::gpu::b200::scan<false, std::uint32_t>(temp, bytes, x, out, n, WrapAdd{}, static_cast<cudaStream_t>(stream));
 }
+#endif
 }

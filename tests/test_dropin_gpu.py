@@ -248,3 +248,104 @@ def test_machine_scan_at_the_bench_size_by_differences(emitted, cuda):
     emitted.b200_scan_u32(torch.cuda.current_stream(cuda).cuda_stream, n, out.data_ptr(), x.data_ptr(), temp.data_ptr())
     torch.cuda.synchronize()
     assert holds()
+
+
+# ---- the same program on the reference's own machine ----------------------------------------------------------------
+REF_DEVICE = Path(__file__).resolve().parents[1] / "baseline" / "_ref" / "libemitted_ref.so"
+
+# Runs in a process of its own (two builds of one program in one process would share their template symbols):
+# argv = library, inputs .npz, outputs .npz. Every entry is the reference machine's (cairn_gpu.hpp, cairn_kernels.hpp,
+# cairn_cub.hpp, cairn_tensor.hpp of the reference tree), reached through the program's cf_ entries.
+_ON_REFERENCE_MACHINE = r"""
+import ctypes as C, sys
+import numpy as np, torch
+h = C.CDLL(sys.argv[1])
+z, p = C.c_size_t, C.c_void_p
+for name, res, args in (("cf_saxpy", None, [z, p, p, p, C.c_float]), ("cf_usum", C.c_uint64, [z, p]),
+                        ("cf_dsum", C.c_float, [z, p]), ("cf_wprefix", C.c_uint32, [z, p, p]),
+                        ("cf_gemm", None, [z, z, z, z, p, z, p, z, p])):
+    f = getattr(h, name)
+    f.restype, f.argtypes = res, args
+d = dict(np.load(sys.argv[2]))
+dev = torch.device("cuda", 0)
+g = lambda a: torch.from_numpy(a).to(dev)
+x, y = g(d["x"]), g(d["y"])
+out = torch.empty_like(x)
+h.cf_saxpy(x.numel(), out.data_ptr(), x.data_ptr(), y.data_ptr(), float(d["a"][0]))
+u = g(d["u"].view(np.int64))
+usum = h.cf_usum(u.numel(), u.data_ptr())
+dsum = h.cf_dsum(x.numel(), x.data_ptr())
+w = g(d["w"].view(np.int32))
+wout = torch.empty_like(w)
+wtotal = h.cf_wprefix(w.numel(), wout.data_ptr(), w.data_ptr())
+m, n, k = (int(v) for v in d["mnk"])
+a, b, c = g(d["ga"].view(np.int16)), g(d["gb"].view(np.int16)), g(d["gc"])
+h.cf_gemm(m, n, k, m * n, c.data_ptr(), m * k, a.data_ptr(), k * n, b.data_ptr())
+torch.cuda.synchronize()
+np.savez(sys.argv[3], saxpy=out.cpu().numpy(), usum=np.asarray([usum], np.uint64),
+         dsum=np.asarray([dsum], np.float32), wprefix=wout.cpu().numpy().view(np.uint32),
+         wtotal=np.asarray([wtotal], np.uint32), gemm=c.cpu().numpy())
+"""
+
+
+def test_the_program_on_the_reference_machine_agrees_with_the_b200_machine(emitted, cuda, tmp_path):
+    """The emitted program built over the reference's headers alone (the reference's lane kernels, CUB collectors
+    and WMMA multiply, compiled for sm_100a) and over the drop-in headers: saxpy, the checked u64 sum and the
+    add_wrap scan give the same bits on both machines and the oracle; the f32 `reduce +` lies within
+    n * 2^-24 * sum |x| of the exact sum on both (the device fold's order is unspecified, docs/numerics.md); the
+    multiply within twice its contract bound on both."""
+    import subprocess
+    import sys
+
+    if not REF_DEVICE.exists():
+        pytest.skip("baseline/_ref/libemitted_ref.so is not built (it needs the CAIRN reference's headers)")
+    rng = np.random.default_rng(77)
+    x_np, y_np, a = inputs.saxpy_case((1 << 22) + 3, seed=5)
+    u_np = np.arange(1_000_003, dtype=np.uint64)
+    w_np = rng.integers(0, 2**32, 3_000_017, dtype=np.uint64).astype(np.uint32)
+    m, n, k = 256, 512, 1024
+    ga = inputs.encode("bf16", rng.standard_normal(m * k))
+    gb = inputs.encode("bf16", rng.standard_normal(k * n))
+    gc = rng.uniform(-2, 2, m * n).astype(np.float32)
+    src = tmp_path / "in.npz"
+    np.savez(src, x=x_np, y=y_np, a=np.asarray([a], np.float32), u=u_np, w=w_np, mnk=np.asarray([m, n, k]), ga=ga,
+             gb=gb, gc=gc)
+    dst = tmp_path / "out.npz"
+    done = subprocess.run([sys.executable, "-c", _ON_REFERENCE_MACHINE, str(REF_DEVICE), str(src), str(dst)],
+                          capture_output=True, text=True, timeout=600)
+    assert done.returncode == 0, done.stderr[-3000:]
+    ref = np.load(dst)
+
+    # this project's machine, the same entries
+    x, y = torch.from_numpy(x_np).to(cuda), torch.from_numpy(y_np).to(cuda)
+    out = torch.empty_like(x)
+    emitted.cf_saxpy(x.numel(), out.data_ptr(), x.data_ptr(), y.data_ptr(), float(a))
+    want = restated.saxpy(float(a), x_np, y_np).view(np.uint32)
+    assert np.array_equal(ref["saxpy"].view(np.uint32), want)
+    assert np.array_equal(out.cpu().numpy().view(np.uint32), want)
+
+    u = torch.from_numpy(u_np.view(np.int64)).to(cuda)
+    assert int(ref["usum"][0]) == emitted.cf_usum(u.numel(), u.data_ptr()) == u_np.size * (u_np.size - 1) // 2
+
+    exact = float(restated.sum_f32(x_np))
+    bound = x_np.size * 2.0**-24 * float(np.abs(x_np.astype(np.float64)).sum())
+    assert abs(float(ref["dsum"][0]) - exact) <= bound
+    assert abs(emitted.cf_dsum(x.numel(), x.data_ptr()) - exact) <= bound
+
+    w = torch.from_numpy(w_np.view(np.int32)).to(cuda)
+    wout = torch.empty_like(w)
+    total = emitted.cf_wprefix(w.numel(), wout.data_ptr(), w.data_ptr())
+    want_scan, want_total = restated.scan_u32(w_np)
+    assert np.array_equal(ref["wprefix"], want_scan) and int(ref["wtotal"][0]) == want_total
+    assert np.array_equal(wout.cpu().numpy().view(np.uint32), want_scan) and total == want_total
+
+    ct = torch.from_numpy(gc.copy()).to(cuda)
+    at = torch.from_numpy(ga.view(np.int16).copy()).to(cuda)
+    bt = torch.from_numpy(gb.view(np.int16).copy()).to(cuda)
+    emitted.cf_gemm(m, n, k, m * n, ct.data_ptr(), m * k, at.data_ptr(), k * n, bt.data_ptr())
+    want_c = restated.mma("bf16", gc, ga, gb, m, n, k).reshape(m, n)
+    av = np.abs(inputs.decode("bf16", ga).reshape(m, k))
+    bv = np.abs(inputs.decode("bf16", gb).reshape(k, n))
+    tol = 2 * (k + 1) * 2.0**-22 * (np.abs(gc.reshape(m, n)) + av @ bv)
+    assert (np.abs(ref["gemm"].reshape(m, n) - want_c) <= tol).all()
+    assert (np.abs(ct.cpu().numpy().reshape(m, n) - want_c) <= tol).all()
