@@ -376,10 +376,20 @@ __device__ __forceinline__ std::uint32_t keep_where_positive(std::uint32_t out2,
   return kept;
 }
 
+// bias_s: the chunk's 32 bias values staged in shared memory (16-byte aligned), or null to read them from p.bias.
 __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int col, const std::uint32_t (&r)[32],
-                                                float (&v)[32], bool apply_mask) {
+                                                float (&v)[32], bool apply_mask, const float* bias_s) {
   float bias[32];
-  if (p.bias != nullptr && col + 32 <= p.n && (reinterpret_cast<std::uintptr_t>(p.bias + col) & 15u) == 0) {
+  if (bias_s != nullptr) {
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const float4 b = reinterpret_cast<const float4*>(bias_s)[q];
+      bias[4 * q] = b.x;
+      bias[4 * q + 1] = b.y;
+      bias[4 * q + 2] = b.z;
+      bias[4 * q + 3] = b.w;
+    }
+  } else if (p.bias != nullptr && col + 32 <= p.n && (reinterpret_cast<std::uintptr_t>(p.bias + col) & 15u) == 0) {
     const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -420,14 +430,14 @@ __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int 
 //   which would serialise the passes on the load's latency.
 template <bool LOADS>
 __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, int col, const std::uint32_t (&r)[32],
-                                                   std::uint8_t* stage, int lane) {
+                                                   std::uint8_t* stage, int lane, const float* bias_s) {
   const int seg = lane & 3, sub = lane >> 2;  // read-back: 4 threads per row (16 bytes each), 8 rows per pass
   if (p.out_kind == OUT_BF16) {
     const bool late_mask = LOADS && p.mask != nullptr && p.vec && p.mask_vec;
     uint4* mine = reinterpret_cast<uint4*>(stage + lane * STAGE_PITCH);
     if constexpr (!LOADS) {
       float v[32];
-      epilogue_values(p, row0 + lane, col, r, v, true);
+      epilogue_values(p, row0 + lane, col, r, v, true, bias_s);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         uint4 w;
@@ -451,9 +461,11 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float b[8];
-        if (bias_vec) {
-          const float4 b0 = __ldg(reinterpret_cast<const float4*>(p.bias + col) + 2 * q);
-          const float4 b1 = __ldg(reinterpret_cast<const float4*>(p.bias + col) + 2 * q + 1);
+        if (bias_s != nullptr || bias_vec) {
+          const float4* src = bias_s != nullptr ? reinterpret_cast<const float4*>(bias_s)
+                                                : reinterpret_cast<const float4*>(p.bias + col);
+          const float4 b0 = bias_s != nullptr ? src[2 * q] : __ldg(src + 2 * q);
+          const float4 b1 = bias_s != nullptr ? src[2 * q + 1] : __ldg(src + 2 * q + 1);
           b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z, b[7] = b1.w;
         } else {
 #pragma unroll
@@ -643,7 +655,8 @@ template <int G> struct PairShape {
   static constexpr int EPI_WARPS = 8;                               // two warps per TMEM lane quarter
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int TILE_N = G * PAIR_BN;
-  static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_HALF) + 256 + EPI_WARPS * STAGE_BYTES;
+  static constexpr int BIAS_BYTES = 1024;  // an epilogue warp's staged bias: up to 256 columns of f32
+  static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_HALF) + 256 + EPI_WARPS * (STAGE_BYTES + BIAS_BYTES);
 };
 
 template <int FMT, int G, bool READS>
@@ -675,6 +688,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
   std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(published + 1);
   volatile std::uint32_t* abort_flag = tmem_slot + 1;
   std::uint8_t* epi_stage = reinterpret_cast<std::uint8_t*>(bars) + 256;  // EPI_WARPS buffers of STAGE_BYTES
+  float* epi_bias = reinterpret_cast<float*>(epi_stage + S::EPI_WARPS * STAGE_BYTES);  // EPI_WARPS x BIAS_BYTES
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const std::uint32_t rank = cluster_rank();
@@ -820,6 +834,17 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       tile_of(t, num_m, num_n, mb, nb);
       const int row0 = mb * 2 * HALF + static_cast<int>(rank) * HALF + quarter * 32;
       const int c_first = nb * S::TILE_N + col0;  // this warp's first output column of the tile
+      // The tile's bias for this warp's columns, staged in shared memory while the MMAs run: read from global
+      // memory chunk by chunk during the drain, each chunk's bias waited on L2 (shared memory leaves L1 little room),
+      // and the next tile's MMAs wait for the drain. (The drain of the tile before has finished with the buffer.)
+      float* bias_s = p.bias != nullptr ? epi_bias + ew * (S::BIAS_BYTES / 4) : nullptr;
+      if (bias_s != nullptr) {
+        for (int i = lane; i < COLS_PER_WARP; i += 32) {
+          const int c = c_first + i;
+          bias_s[i] = c < p.n ? __ldg(p.bias + c) : 0.0f;
+        }
+        __syncwarp();
+      }
       if constexpr (READS) {
         if (p.mask != nullptr)
           prefetch_row_span(p.mask, 2, p, row0 + lane, c_first, c_first + COLS_PER_WARP);
@@ -842,7 +867,8 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
             __stcg(dst + q * 32, make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
                                              __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
         } else {
-          store_chunk_staged<READS>(p, row0, nb * S::TILE_N + col0 + ci * 32, r, stage, lane);
+          store_chunk_staged<READS>(p, row0, nb * S::TILE_N + col0 + ci * 32, r, stage, lane,
+                                    bias_s != nullptr ? bias_s + ci * 32 : nullptr);
         }
       };
       if constexpr (READS) {
@@ -948,7 +974,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
         tile_of(tt, num_m, num_n, mb, nb);
         const int w_quarter = (w + 2) & 3;  // epilogue warp w is warp w + 2: its TMEM lane quarter
         store_chunk_staged<READS>(p, mb * 2 * HALF + rr * HALF + w_quarter * 32,
-                           nb * S::TILE_N + (w / 4) * COLS_PER_WARP + ci * 32, r, stage, lane);
+                                  nb * S::TILE_N + (w / 4) * COLS_PER_WARP + ci * 32, r, stage, lane, nullptr);
       }
     }
   }
