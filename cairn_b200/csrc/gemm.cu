@@ -55,6 +55,7 @@ struct TcParams {
   int act;
   const std::uint16_t* mask;  // OUT_BF16 only: keep an output where this m x n bf16 array is > 0, else 0
   int mask_vec;               // mask starts on 16 bytes (its rows then do too whenever vec holds)
+  int tma_store;              // pair kernel, bf16 out: chunks leave through the output's tensor map (TMA stores)
   int vec;        // every output row starts on 16 bytes and holds whole 16-byte groups
   std::uint32_t* fault;
   int streamk;            // split the tiles' k-blocks evenly over the pairs (pair kernel only)
@@ -430,8 +431,43 @@ __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int 
 //   which would serialise the passes on the load's latency.
 template <bool LOADS>
 __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, int col, const std::uint32_t (&r)[32],
-                                                   std::uint8_t* stage, int lane, const float* bias_s) {
+                                                   std::uint8_t* stage, int lane, const float* bias_s,
+                                                   const CUtensorMap* tm_c) {
   const int seg = lane & 3, sub = lane >> 2;  // read-back: 4 threads per row (16 bytes each), 8 rows per pass
+  if constexpr (!LOADS) {
+    if (p.out_kind == OUT_BF16 && p.tma_store) {
+      // The chunk leaves through the output's tensor map: the warp writes it once into its buffer as 32 rows of 64
+      // bytes, 64-byte swizzled (row r's 16-byte group q at r 64 + 16 (q ^ ((r >> 1) & 3)), which spreads each
+      // quarter-warp's writes over all 32 banks), and one lane hands it to a TMA store, which clips rows and columns
+      // outside the output and leaves the warp free. The buffer is rewritten only once the previous chunk's store
+      // has read it.
+      float v[32];
+      epilogue_values(p, row0 + lane, col, r, v, true, bias_s);
+      if (lane == 0) bulk_wait_read();
+      __syncwarp();
+      std::uint8_t* mine = stage + lane * 64;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint4 w;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(v[8 * q + 0], v[8 * q + 1]);
+        __nv_bfloat162 h1 = __floats2bfloat162_rn(v[8 * q + 2], v[8 * q + 3]);
+        __nv_bfloat162 h2 = __floats2bfloat162_rn(v[8 * q + 4], v[8 * q + 5]);
+        __nv_bfloat162 h3 = __floats2bfloat162_rn(v[8 * q + 6], v[8 * q + 7]);
+        std::memcpy(&w.x, &h0, 4);
+        std::memcpy(&w.y, &h1, 4);
+        std::memcpy(&w.z, &h2, 4);
+        std::memcpy(&w.w, &h3, 4);
+        *reinterpret_cast<uint4*>(mine + 16 * (q ^ ((lane >> 1) & 3))) = w;
+      }
+      fence_proxy_async_shared();
+      __syncwarp();
+      if (lane == 0) {
+        tma_store_2d(tm_c, smem_u32(stage), col, row0);
+        bulk_commit();
+      }
+      return;
+    }
+  }
   if (p.out_kind == OUT_BF16) {
     const bool late_mask = LOADS && p.mask != nullptr && p.vec && p.mask_vec;
     uint4* mine = reinterpret_cast<uint4*>(stage + lane * STAGE_PITCH);
@@ -656,13 +692,13 @@ template <int G> struct PairShape {
   static constexpr int THREADS = 64 + 32 * EPI_WARPS;
   static constexpr int TILE_N = G * PAIR_BN;
   static constexpr int BIAS_BYTES = 1024;  // an epilogue warp's staged bias: up to 256 columns of f32
-  static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_HALF) + 256 + EPI_WARPS * (STAGE_BYTES + BIAS_BYTES);
+  static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_HALF) + 1024 + EPI_WARPS * (STAGE_BYTES + BIAS_BYTES);
 };
 
 template <int FMT, int G, bool READS>
 __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                        const TcParams p) {
+                        const __grid_constant__ CUtensorMap tm_c, const TcParams p) {
   using F = Fmt<FMT>;
   using S = PairShape<G>;
   constexpr int STAGES = S::STAGES;
@@ -687,7 +723,9 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
   std::uint64_t* published = drain + 1;  // every epilogue warp of this CTA has written its stream-K partial
   std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(published + 1);
   volatile std::uint32_t* abort_flag = tmem_slot + 1;
-  std::uint8_t* epi_stage = reinterpret_cast<std::uint8_t*>(bars) + 256;  // EPI_WARPS buffers of STAGE_BYTES
+  // EPI_WARPS buffers of STAGE_BYTES, from 1024 bytes past the barriers: each starts on 512 bytes (STAGE_BYTES is a
+  // multiple), as a TMA store's 64-byte-swizzled source must.
+  std::uint8_t* epi_stage = reinterpret_cast<std::uint8_t*>(bars) + 1024;
   float* epi_bias = reinterpret_cast<float*>(epi_stage + S::EPI_WARPS * STAGE_BYTES);  // EPI_WARPS x BIAS_BYTES
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -868,7 +906,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
                                              __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
         } else {
           store_chunk_staged<READS>(p, row0, nb * S::TILE_N + col0 + ci * 32, r, stage, lane,
-                                    bias_s != nullptr ? bias_s + ci * 32 : nullptr);
+                                    bias_s != nullptr ? bias_s + ci * 32 : nullptr, &tm_c);
         }
       };
       if constexpr (READS) {
@@ -974,9 +1012,11 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
         tile_of(tt, num_m, num_n, mb, nb);
         const int w_quarter = (w + 2) & 3;  // epilogue warp w is warp w + 2: its TMEM lane quarter
         store_chunk_staged<READS>(p, mb * 2 * HALF + rr * HALF + w_quarter * 32,
-                                  nb * S::TILE_N + (w / 4) * COLS_PER_WARP + ci * 32, r, stage, lane, nullptr);
+                                  nb * S::TILE_N + (w / 4) * COLS_PER_WARP + ci * 32, r, stage, lane, nullptr,
+                                  &tm_c);
       }
     }
+    if (p.tma_store && lane == 0) bulk_wait();  // this warp's TMA stores are complete before the CTA ends
   }
 
   tc_fence_before();
@@ -1136,6 +1176,20 @@ bool encode(CUtensorMap* map, int fmt, const void* base, std::uint64_t cols, std
 
 int esize_of(int fmt) { return fmt == FMT_TF32 ? 4 : (fmt == FMT_E4M3 || fmt == FMT_E5M2) ? 1 : 2; }
 
+// The pair kernel's bf16 output as the target of TMA stores: boxes of 32 x 32 elements (one epilogue chunk), 64-byte
+// swizzled. Needs the output on 16 bytes and rows of whole 16-byte groups (n a multiple of 8).
+bool encode_out_bf16(CUtensorMap* map, void* out, std::uint64_t n, std::uint64_t m) {
+  EncodeTiled fn = encoder();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {n, m};
+  const cuuint64_t strides[1] = {n * 2};
+  const cuuint32_t box[2] = {32, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
 
 // Which tile runs: 0 the one-SM 128 x BN tile, 1 the pair's 256 x 256, 2 the pair's 256 x 512. The pair tiles pay
@@ -1271,6 +1325,16 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   // Epilogues that read memory (the ReLU-gradient mask, the accumulate form's old outputs) run their own
   // instantiation, whose drain keeps those loads in flight; the others keep the double-buffered TMEM drain.
   const bool reads = p.mask != nullptr || p.out_kind == OUT_ACC_F32;
+  // A bf16 output of an epilogue that reads no memory leaves through TMA stores where the tensor map allows.
+  // CAIRN_B200_TMA_STORE=0 keeps the threads' own stores (for measuring one against the other).
+  static const bool tma_store_on = [] {
+    const char* v = std::getenv("CAIRN_B200_TMA_STORE");
+    return !(v && v[0] == '0');
+  }();
+  CUtensorMap tc;
+  std::memset(&tc, 0, sizeof(tc));
+  const int tma_store = (tma_store_on && !reads && g.out_kind == OUT_BF16 && p.vec &&
+                         encode_out_bf16(&tc, g.out, g.n, g.m)) ? 1 : 0;
   cudaError_t e = reads ? configure_pair<FMT, G, true>() : configure_pair<FMT, G, false>();
   if (e != cudaSuccess) return e;
   const int tiles = ((p.m + 2 * HALF - 1) / (2 * HALF)) * ((p.n + S::TILE_N - 1) / S::TILE_N);
@@ -1283,6 +1347,7 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   q.flags = static_cast<std::uint32_t*>(g.ws);  // the workspace: the barrier's arrival counter, then the slots
   q.ws = g.ws ? reinterpret_cast<float*>(static_cast<char*>(g.ws) + 256) : nullptr;
   q.epoch = g.epoch;
+  q.tma_store = tma_store;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(2 * pairs, 1, 1);
   cfg.blockDim = dim3(S::THREADS, 1, 1);
@@ -1295,8 +1360,8 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = reads ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, true>, ta, tb, q)
-            : cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, false>, ta, tb, q);
+  e = reads ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, true>, ta, tb, tc, q)
+            : cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, false>, ta, tb, tc, q);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

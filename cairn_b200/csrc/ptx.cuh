@@ -223,6 +223,23 @@ __device__ __forceinline__ void tma_load_2d_pair(std::uint32_t dst, const CUtens
       "l"(reinterpret_cast<std::uint64_t>(map)), "r"(cluster_bar), "r"(x), "r"(y)
       : "memory");
 }
+// TMA store of a box from this CTA's shared memory into the tensor at (x, y), in the thread's bulk group; elements
+// outside the tensor's extents are not written. Shared-memory writes made through the generic proxy must be fenced
+// (fence_proxy_async_shared) before the store reads them.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, std::uint32_t src, std::int32_t x, std::int32_t y) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<std::uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until every committed bulk store of this thread has read its shared-memory source (the buffer is free).
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until every committed bulk store of this thread has completed.
+__device__ __forceinline__ void bulk_wait() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 __device__ __forceinline__ void tmem_alloc_pair(std::uint32_t* slot, std::uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)), "r"(cols)
                : "memory");
