@@ -55,7 +55,7 @@ struct TcParams {
   int act;
   const std::uint16_t* mask;  // OUT_BF16 only: keep an output where this m x n bf16 array is > 0, else 0
   int mask_vec;               // mask starts on 16 bytes (its rows then do too whenever vec holds)
-  int tma_store;              // pair kernel, bf16 out: chunks leave through the output's tensor map (TMA stores)
+  int tma_store;              // pair kernel, bf16 or stored f32 out: chunks leave through TMA stores
   int vec;        // every output row starts on 16 bytes and holds whole 16-byte groups
   std::uint32_t* fault;
   int streamk;            // split the tiles' k-blocks evenly over the pairs (pair kernel only)
@@ -464,6 +464,27 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
       if (lane == 0) {
         tma_store_2d(tm_c, smem_u32(stage), col, row0);
         bulk_commit();
+      }
+      return;
+    }
+    if (p.out_kind == OUT_STORE_F32 && p.tma_store) {
+      // f32 outputs the same way, a 16-column half (32 rows of 64 bytes) at a time.
+      std::uint8_t* mine = stage + lane * 64;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        if (lane == 0) bulk_wait_read();
+        __syncwarp();
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<float4*>(mine + 16 * (q ^ ((lane >> 1) & 3))) =
+              make_float4(__uint_as_float(r[16 * half + 4 * q]), __uint_as_float(r[16 * half + 4 * q + 1]),
+                          __uint_as_float(r[16 * half + 4 * q + 2]), __uint_as_float(r[16 * half + 4 * q + 3]));
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(tm_c, smem_u32(stage), col + 16 * half, row0);
+          bulk_commit();
+        }
       }
       return;
     }
@@ -1176,18 +1197,18 @@ bool encode(CUtensorMap* map, int fmt, const void* base, std::uint64_t cols, std
 
 int esize_of(int fmt) { return fmt == FMT_TF32 ? 4 : (fmt == FMT_E4M3 || fmt == FMT_E5M2) ? 1 : 2; }
 
-// The pair kernel's bf16 output as the target of TMA stores: boxes of 32 x 32 elements (one epilogue chunk), 64-byte
-// swizzled. Needs the output on 16 bytes and rows of whole 16-byte groups (n a multiple of 8).
-bool encode_out_bf16(CUtensorMap* map, void* out, std::uint64_t n, std::uint64_t m) {
+// The pair kernel's output as the target of TMA stores: boxes of 32 rows of 64 bytes (a bf16 epilogue chunk, or
+// half of an f32 one), 64-byte swizzled. Needs the output on 16 bytes and rows of whole 16-byte groups.
+bool encode_out(CUtensorMap* map, void* out, std::uint64_t n, std::uint64_t m, bool f32) {
   EncodeTiled fn = encoder();
   if (!fn) return false;
   const cuuint64_t dims[2] = {n, m};
-  const cuuint64_t strides[1] = {n * 2};
-  const cuuint32_t box[2] = {32, 32};
+  const cuuint64_t strides[1] = {n * (f32 ? 4 : 2)};
+  const cuuint32_t box[2] = {f32 ? 16u : 32u, 32};
   const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
-         CUDA_SUCCESS;
+  return fn(map, f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides, box,
+            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0; }
@@ -1325,7 +1346,8 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   // Epilogues that read memory (the ReLU-gradient mask, the accumulate form's old outputs) run their own
   // instantiation, whose drain keeps those loads in flight; the others keep the double-buffered TMEM drain.
   const bool reads = p.mask != nullptr || p.out_kind == OUT_ACC_F32;
-  // A bf16 output of an epilogue that reads no memory leaves through TMA stores where the tensor map allows.
+  // The output of an epilogue that reads no memory (bf16, or f32 stored) leaves through TMA stores where the
+  // tensor map allows.
   // CAIRN_B200_TMA_STORE=0 keeps the threads' own stores (for measuring one against the other).
   static const bool tma_store_on = [] {
     const char* v = std::getenv("CAIRN_B200_TMA_STORE");
@@ -1333,8 +1355,8 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   }();
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
-  const int tma_store = (tma_store_on && !reads && g.out_kind == OUT_BF16 && p.vec &&
-                         encode_out_bf16(&tc, g.out, g.n, g.m)) ? 1 : 0;
+  const int tma_store = (tma_store_on && !reads && (g.out_kind == OUT_BF16 || g.out_kind == OUT_STORE_F32) &&
+                         p.vec && encode_out(&tc, g.out, g.n, g.m, g.out_kind == OUT_STORE_F32)) ? 1 : 0;
   cudaError_t e = reads ? configure_pair<FMT, G, true>() : configure_pair<FMT, G, false>();
   if (e != cudaSuccess) return e;
   const int tiles = ((p.m + 2 * HALF - 1) / (2 * HALF)) * ((p.n + S::TILE_N - 1) / S::TILE_N);
