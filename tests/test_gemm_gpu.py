@@ -143,9 +143,12 @@ def _bf16_close(got_bits: np.ndarray, want_bits: np.ndarray, acc_tol: np.ndarray
 
 
 @pytest.mark.parametrize("relu", [True, False])
-def test_fused_bias_relu_bf16_epilogue(cuda, relu):
-    """bf16(act(acc + bias)): within one bf16 rounding of the oracle's epilogue on its own accumulator."""
-    m, n, k = 384, 520, 256
+@pytest.mark.parametrize("shape", [(384, 520, 256), (300, 264, 136), (520, 776, 72)])
+def test_fused_bias_relu_bf16_epilogue(cuda, relu, shape):
+    """bf16(act(acc + bias)): within one bf16 rounding of the oracle's epilogue on its own accumulator. The shapes
+    leave partial tiles in both directions, on the 256 x 512 and the 256 x 256 pair tiles, whose chunks the TMA
+    stores clip at the output's edges."""
+    m, n, k = shape
     rng = np.random.default_rng(8)
     a = inputs.encode("bf16", rng.standard_normal(m * k))
     b = inputs.encode("bf16", rng.standard_normal(k * n))
@@ -305,3 +308,21 @@ def test_relu_grad_is_the_product_kept_where_the_forward_was_positive(cuda, m, n
     want = np.where(positive, plain_bits, np.uint16(0))
     bad = np.flatnonzero(got_bits != want)
     assert bad.size == 0, (bad[:4], got_bits[bad[:4]], want[bad[:4]], mask[bad[:4]])
+
+
+@pytest.mark.parametrize("shape", [(300, 776, 136), (520, 264, 72), (257, 512, 64)])
+def test_stored_f32_products_with_partial_tiles(cuda, shape):
+    """C = A B stored as f32 (no old value read) on shapes whose last row band and column tile are partial: the
+    chunks leave through TMA stores in 16-column halves, clipped at the output's edges; every element within twice
+    the contract bound of the oracle."""
+    m, n, k = shape
+    rng = np.random.default_rng(m + n)
+    a = inputs.encode("bf16", rng.standard_normal(m * k))
+    b = inputs.encode("bf16", rng.standard_normal(k * n))
+    at, bt = to_dev("bf16", a, cuda).view(m, k), to_dev("bf16", b, cuda).view(k, n)
+    out = torch.full((m, n), float("nan"), device=cuda)
+    cairn_b200.gemm(at, bt, out=out)
+    cairn_b200.stream_status()
+    zero = np.zeros(m * n, np.float32)
+    want = restated.mma("bf16", zero, a, b, m, n, k)
+    assert within(out.cpu().numpy().ravel(), want, 2 * bound("bf16", zero, a, b, m, n, k)).all()
