@@ -55,7 +55,7 @@ struct TcParams {
   int act;
   const std::uint16_t* mask;  // OUT_BF16 only: keep an output where this m x n bf16 array is > 0, else 0
   int mask_vec;               // mask starts on 16 bytes (its rows then do too whenever vec holds)
-  int tma_store;              // pair kernel, bf16 or stored f32 out: chunks leave through TMA stores
+  int tma_store;              // pair kernel: chunks leave through TMA stores (1), or TMA reduce-adds into C (2)
   int vec;        // every output row starts on 16 bytes and holds whole 16-byte groups
   std::uint32_t* fault;
   int streamk;            // split the tiles' k-blocks evenly over the pairs (pair kernel only)
@@ -467,8 +467,10 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
       }
       return;
     }
-    if (p.out_kind == OUT_STORE_F32 && p.tma_store) {
-      // f32 outputs the same way, a 16-column half (32 rows of 64 bytes) at a time.
+    if ((p.out_kind == OUT_STORE_F32 || p.out_kind == OUT_ACC_F32) && p.tma_store) {
+      // f32 outputs the same way, a 16-column half (32 rows of 64 bytes) at a time. The accumulate form (C += A B)
+      // hands the half to a TMA reduce-add: L2 adds it to C element by element, each sum rounded once to nearest,
+      // as old + acc rounded in the epilogue would be; one tile owns each element, so each is added once.
       std::uint8_t* mine = stage + lane * 64;
 #pragma unroll
       for (int half = 0; half < 2; ++half) {
@@ -482,7 +484,10 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
         fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0) {
-          tma_store_2d(tm_c, smem_u32(stage), col + 16 * half, row0);
+          if (p.tma_store == 2)
+            tma_reduce_add_2d(tm_c, smem_u32(stage), col + 16 * half, row0);
+          else
+            tma_store_2d(tm_c, smem_u32(stage), col + 16 * half, row0);
           bulk_commit();
         }
       }
@@ -1343,20 +1348,21 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   const bool ok_b = g.trans_b ? encode(&tb, FMT, g.b, g.k, g.n, es, CH, HALF, false)
                               : encode(&tb, FMT, g.b, g.n, g.k, es, CH, CH, true);
   if (!ok_a || !ok_b) return cudaErrorInvalidValue;
-  // Epilogues that read memory (the ReLU-gradient mask, the accumulate form's old outputs) run their own
-  // instantiation, whose drain keeps those loads in flight; the others keep the double-buffered TMEM drain.
-  const bool reads = p.mask != nullptr || p.out_kind == OUT_ACC_F32;
-  // The output of an epilogue that reads no memory (bf16, or f32 stored) leaves through TMA stores where the
-  // tensor map allows.
-  // CAIRN_B200_TMA_STORE=0 keeps the threads' own stores (for measuring one against the other).
+  // Outputs leave through TMA stores where the output's tensor map allows (bf16, f32 stored, and f32 accumulated,
+  // which becomes a TMA reduce-add into C), except under the ReLU-gradient mask. Epilogues that still read memory (the
+  // mask; the accumulate form off the tensor-map rules) run their own instantiation, whose drain keeps those loads
+  // in flight; the others keep the double-buffered TMEM drain. CAIRN_B200_TMA_STORE=0 keeps the threads' own stores
+  // and loads (for measuring one against the other).
   static const bool tma_store_on = [] {
     const char* v = std::getenv("CAIRN_B200_TMA_STORE");
     return !(v && v[0] == '0');
   }();
   CUtensorMap tc;
   std::memset(&tc, 0, sizeof(tc));
-  const int tma_store = (tma_store_on && !reads && (g.out_kind == OUT_BF16 || g.out_kind == OUT_STORE_F32) &&
-                         p.vec && encode_out(&tc, g.out, g.n, g.m, g.out_kind == OUT_STORE_F32)) ? 1 : 0;
+  const bool f32_out = g.out_kind != OUT_BF16;
+  const bool tma_ok = tma_store_on && p.mask == nullptr && p.vec && encode_out(&tc, g.out, g.n, g.m, f32_out);
+  const int tma_store = tma_ok ? (g.out_kind == OUT_ACC_F32 ? 2 : 1) : 0;
+  const bool reads = p.mask != nullptr || (p.out_kind == OUT_ACC_F32 && !tma_ok);
   cudaError_t e = reads ? configure_pair<FMT, G, true>() : configure_pair<FMT, G, false>();
   if (e != cudaSuccess) return e;
   const int tiles = ((p.m + 2 * HALF - 1) / (2 * HALF)) * ((p.n + S::TILE_N - 1) / S::TILE_N);

@@ -232,6 +232,14 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, std::uint32
                "r"(src), "r"(x), "r"(y)
                : "memory");
 }
+// The same box added element by element into the tensor (f32 add, rounded to nearest), in the thread's bulk group.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, std::uint32_t src, std::int32_t x,
+                                                  std::int32_t y) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<std::uint64_t>(map)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Waits until every committed bulk store of this thread has read its shared-memory source (the buffer is free).
 __device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
