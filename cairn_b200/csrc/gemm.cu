@@ -55,7 +55,8 @@ struct TcParams {
   int act;
   const std::uint16_t* mask;  // OUT_BF16 only: keep an output where this m x n bf16 array is > 0, else 0
   int mask_vec;               // mask starts on 16 bytes (its rows then do too whenever vec holds)
-  int tma_store;              // pair kernel: chunks leave through TMA stores (1), or TMA reduce-adds into C (2)
+  int tma_store;              // pair kernel: chunks leave through TMA stores (1), TMA reduce-adds into C (2), or
+                              // TMA stores of bf16 outputs masked by the mask's tiles, which come in by TMA (3)
   int vec;        // every output row starts on 16 bytes and holds whole 16-byte groups
   std::uint32_t* fault;
   int streamk;            // split the tiles' k-blocks evenly over the pairs (pair kernel only)
@@ -429,10 +430,19 @@ __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int 
 //   per 8 outputs, and the accumulate form's old values likewise, a half's four at once. Both kinds of load are
 //   issued together before the first store: a load after a store to the output could not be moved above it,
 //   which would serialise the passes on the load's latency.
-template <bool LOADS>
+// The TMA mask path's per-warp state: the warp's mbarrier for its mask tiles, the parity of the next, and the abort
+// flag its bounded wait watches.
+struct MaskTiles {
+  const CUtensorMap* map;
+  std::uint64_t* bar;
+  std::uint32_t phase;
+  volatile std::uint32_t* abort_flag;
+};
+
+template <bool LOADS, bool MASKED>
 __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, int col, const std::uint32_t (&r)[32],
                                                    std::uint8_t* stage, int lane, const float* bias_s,
-                                                   const CUtensorMap* tm_c) {
+                                                   const CUtensorMap* tm_c, MaskTiles& mt) {
   const int seg = lane & 3, sub = lane >> 2;  // read-back: 4 threads per row (16 bytes each), 8 rows per pass
   if constexpr (!LOADS) {
     if (p.out_kind == OUT_BF16 && p.tma_store) {
@@ -441,10 +451,25 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
       // quarter-warp's writes over all 32 banks), and one lane hands it to a TMA store, which clips rows and columns
       // outside the output and leaves the warp free. The buffer is rewritten only once the previous chunk's store
       // has read it.
+      // The ReLU-gradient mask (mode 3): lane 0 asks TMA for the chunk's 32 x 32 mask tile into the buffer, laid out
+      // as the output will be, as soon as the previous chunk's store has read the buffer; the warp forms its values
+      // meanwhile, then each thread masks its own row in place (keep_where_positive, the same test as the per-element
+      // one) before the store.
+      constexpr bool masked = MASKED;
+      if (lane == 0) {
+        bulk_wait_read();
+        if (masked) {
+          mbar_arrive_expect_tx(mt.bar, 32 * 64);
+          tma_load_2d(smem_u32(stage), mt.map, mt.bar, col, row0);
+        }
+      }
       float v[32];
-      epilogue_values(p, row0 + lane, col, r, v, true, bias_s);
-      if (lane == 0) bulk_wait_read();
+      epilogue_values(p, row0 + lane, col, r, v, !masked, bias_s);
       __syncwarp();
+      if (masked) {
+        mbar_wait(mt.bar, mt.phase, mt.abort_flag, p.fault, FAULT_WAIT_MASK);
+        mt.phase ^= 1u;
+      }
       std::uint8_t* mine = stage + lane * 64;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
@@ -457,7 +482,15 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
         std::memcpy(&w.y, &h1, 4);
         std::memcpy(&w.z, &h2, 4);
         std::memcpy(&w.w, &h3, 4);
-        *reinterpret_cast<uint4*>(mine + 16 * (q ^ ((lane >> 1) & 3))) = w;
+        uint4* slot = reinterpret_cast<uint4*>(mine + 16 * (q ^ ((lane >> 1) & 3)));
+        if (masked) {
+          const uint4 mk = *slot;
+          w.x = keep_where_positive(w.x, mk.x);
+          w.y = keep_where_positive(w.y, mk.y);
+          w.z = keep_where_positive(w.z, mk.z);
+          w.w = keep_where_positive(w.w, mk.w);
+        }
+        *slot = w;
       }
       fence_proxy_async_shared();
       __syncwarp();
@@ -721,12 +754,18 @@ template <int G> struct PairShape {
   static constexpr int SMEM = 1024 + STAGES * (A_STAGE + B_HALF) + 1024 + EPI_WARPS * (STAGE_BYTES + BIAS_BYTES);
 };
 
-template <int FMT, int G, bool READS>
+// EPI: 0 an epilogue that reads no memory (its chunks leave by TMA stores or reduce-adds, or the threads' stores);
+// 1 one that reads memory through the threads' loads (the mask or old C off the tensor-map rules); 2 bf16 under the
+// ReLU-gradient mask, whose tiles come in by TMA. Each is its own instantiation, so each gets its own registers.
+template <int FMT, int G, int EPI>
 __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
-                        const __grid_constant__ CUtensorMap tm_c, const TcParams p) {
+                        const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_m,
+                        const TcParams p) {
   using F = Fmt<FMT>;
   using S = PairShape<G>;
+  constexpr bool READS = EPI == 1;
+  constexpr bool MASKED = EPI == 2;
   constexpr int STAGES = S::STAGES;
   constexpr int CH = SLICE / F::bytes;
   constexpr int MMA_K_BYTES = 32;
@@ -747,7 +786,8 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
   std::uint64_t* tempty = tfull + 2;
   std::uint64_t* drain = tempty + 2;
   std::uint64_t* published = drain + 1;  // every epilogue warp of this CTA has written its stream-K partial
-  std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(published + 1);
+  std::uint64_t* mask_bars = published + 1;  // one per epilogue warp: its mask tiles' TMA loads (mode 3)
+  std::uint32_t* tmem_slot = reinterpret_cast<std::uint32_t*>(mask_bars + S::EPI_WARPS);
   volatile std::uint32_t* abort_flag = tmem_slot + 1;
   // EPI_WARPS buffers of STAGE_BYTES, from 1024 bytes past the barriers: each starts on 512 bytes (STAGE_BYTES is a
   // multiple), as a TMA store's 64-byte-swizzled source must.
@@ -772,6 +812,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
     }
     mbar_init(drain, 1);
     mbar_init(published, S::EPI_WARPS);
+    for (int w = 0; w < S::EPI_WARPS; ++w) mbar_init(&mask_bars[w], 1);
     *abort_flag = 0u;
     fence_barrier_init();
   }
@@ -888,6 +929,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
     constexpr int CHUNKS = COLS_PER_WARP / 32;
     constexpr std::size_t SLOT = static_cast<std::size_t>(S::EPI_WARPS) * CHUNKS * 32 * 32;  // floats per slot
     std::uint8_t* stage = epi_stage + ew * STAGE_BYTES;
+    MaskTiles mt{&tm_m, &mask_bars[ew], 0u, abort_flag};
     std::uint32_t it = 0;
     PairWork work(pair, pairs, tiles, num_kb, p.streamk != 0);
     int t, kb_begin, kb_end;
@@ -909,7 +951,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
         }
         __syncwarp();
       }
-      if constexpr (READS) {
+      if constexpr (READS || MASKED) {
         if (p.mask != nullptr)
           prefetch_row_span(p.mask, 2, p, row0 + lane, c_first, c_first + COLS_PER_WARP);
         else if (p.out_kind == OUT_ACC_F32 && kb_begin == 0 && kb_end == num_kb)
@@ -931,11 +973,11 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
             __stcg(dst + q * 32, make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
                                              __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
         } else {
-          store_chunk_staged<READS>(p, row0, nb * S::TILE_N + col0 + ci * 32, r, stage, lane,
-                                    bias_s != nullptr ? bias_s + ci * 32 : nullptr, &tm_c);
+          store_chunk_staged<READS, MASKED>(p, row0, nb * S::TILE_N + col0 + ci * 32, r, stage, lane,
+                                    bias_s != nullptr ? bias_s + ci * 32 : nullptr, &tm_c, mt);
         }
       };
-      if constexpr (READS) {
+      if constexpr (READS || MASKED) {
         // An epilogue that reads memory (the ReLU-gradient mask, or the old outputs of the accumulate form) keeps
         // those loads in flight rather than the TMEM loads: single-buffered, so its registers hold a chunk's loads.
 #pragma unroll 1
@@ -1037,9 +1079,9 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
         int mb, nb;
         tile_of(tt, num_m, num_n, mb, nb);
         const int w_quarter = (w + 2) & 3;  // epilogue warp w is warp w + 2: its TMEM lane quarter
-        store_chunk_staged<READS>(p, mb * 2 * HALF + rr * HALF + w_quarter * 32,
+        store_chunk_staged<READS, MASKED>(p, mb * 2 * HALF + rr * HALF + w_quarter * 32,
                                   nb * S::TILE_N + (w / 4) * COLS_PER_WARP + ci * 32, r, stage, lane, nullptr,
-                                  &tm_c);
+                                  &tm_c, mt);
       }
     }
     if (p.tma_store && lane == 0) bulk_wait();  // this warp's TMA stores are complete before the CTA ends
@@ -1289,14 +1331,14 @@ cudaError_t launch_tc(const GemmArgs& g, const TcParams& p, cudaStream_t stream,
 }
 
 // The pair kernel's dynamic shared memory, set once per device and instantiation before its first launch.
-template <int FMT, int G, bool READS> cudaError_t configure_pair() {
+template <int FMT, int G, int EPI> cudaError_t configure_pair() {
   static std::atomic<std::uint64_t> configured{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   const std::uint64_t bit = 1ull << (dev & 63);
   if (configured.load(std::memory_order_acquire) & bit) return cudaSuccess;
-  e = cudaFuncSetAttribute(tc_gemm_pair_kernel<FMT, G, READS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  e = cudaFuncSetAttribute(tc_gemm_pair_kernel<FMT, G, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            PairShape<G>::SMEM);
   if (e != cudaSuccess) return e;
   configured.fetch_or(bit, std::memory_order_acq_rel);
@@ -1313,7 +1355,7 @@ template <int G> int resident_pairs(int sms) {
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
   const int known = cached[dev & 63].load(std::memory_order_acquire);
   if (known) return known;
-  if (configure_pair<FMT_BF16, G, false>() != cudaSuccess) return 0;
+  if (configure_pair<FMT_BF16, G, 0>() != cudaSuccess) return 0;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(sms, 1, 1);
   cfg.blockDim = dim3(PairShape<G>::THREADS, 1, 1);
@@ -1326,7 +1368,7 @@ template <int G> int resident_pairs(int sms) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   int clusters = 0;
-  if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_pair_kernel<FMT_BF16, G, false>, &cfg) != cudaSuccess ||
+  if (cudaOccupancyMaxActiveClusters(&clusters, tc_gemm_pair_kernel<FMT_BF16, G, 0>, &cfg) != cudaSuccess ||
       clusters <= 0) {
     cudaGetLastError();  // leave no sticky error behind for the launch to report
     return 0;
@@ -1348,22 +1390,27 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   const bool ok_b = g.trans_b ? encode(&tb, FMT, g.b, g.k, g.n, es, CH, HALF, false)
                               : encode(&tb, FMT, g.b, g.n, g.k, es, CH, CH, true);
   if (!ok_a || !ok_b) return cudaErrorInvalidValue;
-  // Outputs leave through TMA stores where the output's tensor map allows (bf16, f32 stored, and f32 accumulated,
-  // which becomes a TMA reduce-add into C), except under the ReLU-gradient mask. Epilogues that still read memory (the
-  // mask; the accumulate form off the tensor-map rules) run their own instantiation, whose drain keeps those loads
-  // in flight; the others keep the double-buffered TMEM drain. CAIRN_B200_TMA_STORE=0 keeps the threads' own stores
-  // and loads (for measuring one against the other).
+  // Outputs leave through TMA stores where the output's tensor map allows (bf16, f32 stored, f32 accumulated as a TMA
+  // reduce-add into C, and bf16 under the ReLU-gradient mask, whose tiles come in by TMA). Epilogues off the
+  // tensor-map rules that read memory (the mask, the accumulate form's old C) run their own instantiation, whose drain
+  // keeps those loads in flight; the others keep the double-buffered TMEM drain. CAIRN_B200_TMA_STORE=0 keeps the
+  // threads' own stores and loads (for measuring one against the other).
   static const bool tma_store_on = [] {
     const char* v = std::getenv("CAIRN_B200_TMA_STORE");
     return !(v && v[0] == '0');
   }();
-  CUtensorMap tc;
+  CUtensorMap tc, tm;
   std::memset(&tc, 0, sizeof(tc));
+  std::memset(&tm, 0, sizeof(tm));
   const bool f32_out = g.out_kind != OUT_BF16;
-  const bool tma_ok = tma_store_on && p.mask == nullptr && p.vec && encode_out(&tc, g.out, g.n, g.m, f32_out);
-  const int tma_store = tma_ok ? (g.out_kind == OUT_ACC_F32 ? 2 : 1) : 0;
-  const bool reads = p.mask != nullptr || (p.out_kind == OUT_ACC_F32 && !tma_ok);
-  cudaError_t e = reads ? configure_pair<FMT, G, true>() : configure_pair<FMT, G, false>();
+  const bool tma_ok = tma_store_on && p.vec && encode_out(&tc, g.out, g.n, g.m, f32_out) &&
+                      (p.mask == nullptr ||
+                       (p.mask_vec && encode_out(&tm, const_cast<std::uint16_t*>(g.mask), g.n, g.m, false)));
+  const int tma_store = !tma_ok ? 0 : p.mask != nullptr ? 3 : g.out_kind == OUT_ACC_F32 ? 2 : 1;
+  const bool reads = !tma_ok && (p.mask != nullptr || p.out_kind == OUT_ACC_F32);
+  const int epi = tma_store == 3 ? 2 : reads ? 1 : 0;
+  cudaError_t e = epi == 2 ? configure_pair<FMT, G, 2>() : epi == 1 ? configure_pair<FMT, G, 1>()
+                                                                  : configure_pair<FMT, G, 0>();
   if (e != cudaSuccess) return e;
   const int tiles = ((p.m + 2 * HALF - 1) / (2 * HALF)) * ((p.n + S::TILE_N - 1) / S::TILE_N);
   const int num_kb = (p.k + CH - 1) / CH;
@@ -1388,8 +1435,9 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = reads ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, true>, ta, tb, tc, q)
-            : cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, false>, ta, tb, tc, q);
+  e = epi == 2   ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 2>, ta, tb, tc, tm, q)
+      : epi == 1 ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 1>, ta, tb, tc, tm, q)
+                 : cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 0>, ta, tb, tc, tm, q);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

@@ -21,6 +21,7 @@ enum Fault : std::uint32_t {
   FAULT_DRAIN = 1u << 4,        // the exit path waited for copies or MMAs still in flight
   FAULT_WAIT_PEER = 1u << 5,    // a stream-K CTA waited at the grid barrier for the others' partials
   FAULT_WATCHDOG = 1u << 6,     // the watchdog self-test's wait (on a barrier nothing completes) ran out
+  FAULT_WAIT_MASK = 1u << 7,    // an epilogue warp waited for its ReLU-gradient mask tile's TMA load
 };
 
 // A flag another CTA raises: read with acquire ordering at GPU scope, raised with release ordering.
