@@ -824,11 +824,19 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
   cluster_sync();  // both CTAs' barriers exist before either side's copies or arrivals reach them
   tc_fence_after();
   const std::uint32_t tmem_base = *tmem_slot;
+  // Launched as a programmatic dependent, this CTA may have started on an SM the product before it on the stream has
+  // left while that product still runs: the set-up above touches only this CTA's shared and tensor memory and its
+  // parameters, and no thread reads or writes global memory until that product has completed. The next product may
+  // then start its own set-up wherever an SM comes free.
+  griddep_launch_dependents();
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_a);
+    tma_prefetch_desc(&tm_b);
+  }
+  griddep_wait();
 
   if (warp == 0) {
     if (lane == 0) {
-      tma_prefetch_desc(&tm_a);
-      tma_prefetch_desc(&tm_b);
       std::uint32_t stage = 0, phase = 0;
       PairWork work(pair, pairs, tiles, num_kb, p.streamk != 0);
       int t, kb_begin, kb_end;
@@ -1428,13 +1436,21 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   cfg.blockDim = dim3(S::THREADS, 1, 1);
   cfg.dynamicSmemBytes = S::SMEM;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  // A programmatic dependent launch: the kernel's set-up may overlap the tail of the grid before it on the stream (it
+  // waits for that grid before touching global memory). CAIRN_B200_PDL=0 launches it plainly (for measuring).
+  static const bool pdl_on = [] {
+    const char* v = std::getenv("CAIRN_B200_PDL");
+    return !(v && v[0] == '0');
+  }();
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_on ? 2 : 1;
   e = epi == 2   ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 2>, ta, tb, tc, tm, q)
       : epi == 1 ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 1>, ta, tb, tc, tm, q)
                  : cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 0>, ta, tb, tc, tm, q);

@@ -192,6 +192,17 @@ __device__ __forceinline__ void tmem_wait_ld(std::uint32_t (&r)[32]) {
 }
 
 // ---------------------------------------------------------------------------------------------------------------
+// Programmatic dependent launch. A grid launched with cudaLaunchAttributeProgrammaticStreamSerialization may start
+// while the grid before it on the stream is still running, once every CTA of that grid has issued
+// griddep_launch_dependents (or exited). griddep_wait blocks until the grid before has completed and its memory
+// operations are visible; without the launch attribute both are no-ops.
+// ---------------------------------------------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// ---------------------------------------------------------------------------------------------------------------
 // CTA pairs (a cluster of 2): the two-SM MMA (cta_group::2). Every copy and every arrival targets one CTA.
 // ---------------------------------------------------------------------------------------------------------------
 __device__ __forceinline__ std::uint32_t cluster_rank() {

@@ -326,3 +326,43 @@ def test_stored_f32_products_with_partial_tiles(cuda, shape):
     zero = np.zeros(m * n, np.float32)
     want = restated.mma("bf16", zero, a, b, m, n, k)
     assert within(out.cpu().numpy().ravel(), want, 2 * bound("bf16", zero, a, b, m, n, k)).all()
+
+
+def test_a_chain_of_products_on_one_stream_reads_each_output_after_it_is_written(cuda):
+    """Products queued back to back on one stream, each reading what the one before wrote (and the third overwriting
+    what the second reads), give the same bits as the same chain with the host waiting after every product: a pair
+    launch that starts while the product before it runs touches no operand or output before that product is done."""
+    rng = torch.Generator(device=cuda).manual_seed(21)
+    m = n = 1024
+    a = torch.randn(m, 512, device=cuda, generator=rng).bfloat16()
+    b1 = torch.randn(512, n, device=cuda, generator=rng).bfloat16()
+    b3 = torch.randn(512, n, device=cuda, generator=rng).bfloat16()
+    w = (torch.randn(n, n, device=cuda, generator=rng) * 0.05).bfloat16()
+    bias = (torch.randn(n, device=cuda, generator=rng) * 0.1).float()
+    c1 = torch.empty(m, n, device=cuda, dtype=torch.bfloat16)
+    c2 = torch.empty_like(c1)
+    c3 = torch.empty(n, n, device=cuda)
+
+    def chain(wait: bool):
+        for t in (c1, c2, c3):
+            t.fill_(float("nan"))
+        steps = [
+            lambda: cairn_b200.gemm(a, b1, out=c1, bias=bias, relu=True, out_dtype=torch.bfloat16),
+            lambda: cairn_b200.gemm(c1, w, out=c2, out_dtype=torch.bfloat16),
+            lambda: cairn_b200.gemm(a, b3, out=c1, out_dtype=torch.bfloat16),
+            lambda: cairn_b200.gemm(c2, c1, trans_a=True, out=c3),
+        ]
+        for s in steps:
+            s()
+            if wait:
+                torch.cuda.synchronize(cuda)
+        cairn_b200.stream_status()
+        return c2.view(torch.int16).clone(), c3.view(torch.int32).clone()
+
+    want2, want3 = chain(wait=True)
+    assert not torch.isnan(want3.view(torch.float32)).any()
+    ref2 = (torch.relu(a.float() @ b1.float() + bias).bfloat16().float() @ w.float())
+    assert ((want2.view(torch.bfloat16).float() - ref2).norm() / ref2.norm()).item() < 2e-2
+    for _ in range(5):
+        got2, got3 = chain(wait=False)
+        assert torch.equal(got2, want2) and torch.equal(got3, want3)
