@@ -103,11 +103,17 @@ template <int FMT>
 __device__ __forceinline__ void store_chunk(const TcParams& p, int row, int col, const std::uint32_t (&r)[32]) {
   if (row >= p.m) return;
   if (p.out_kind == OUT_BF16) {
-    float v[32];
+    float v[32], bias[32];
+    if (p.bias == nullptr) {  // zeros, added all the same (-0 becomes +0 as in the biased forms)
+#pragma unroll
+      for (int j = 0; j < 32; ++j) bias[j] = 0.0f;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) bias[j] = col + j < p.n ? __ldg(p.bias + col + j) : 0.0f;
+    }
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
-      const float b = (p.bias != nullptr && col + j < p.n) ? __ldg(p.bias + col + j) : 0.0f;
-      float x = __fadd_rn(__uint_as_float(r[j]), b);
+      float x = __fadd_rn(__uint_as_float(r[j]), bias[j]);
       if (p.act == ACT_RELU) x = x < 0.0f ? 0.0f : x;
       v[j] = x;
     }
@@ -391,7 +397,12 @@ __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int 
       bias[4 * q + 2] = b.z;
       bias[4 * q + 3] = b.w;
     }
-  } else if (p.bias != nullptr && col + 32 <= p.n && (reinterpret_cast<std::uintptr_t>(p.bias + col) & 15u) == 0) {
+  } else if (p.bias == nullptr) {
+    // No bias: zeros, added all the same (x + 0 turns -0 into +0, as the biased forms' arithmetic does). Tested
+    // before any per-element branch, which costs the drain several hundred cycles per chunk for loads never made.
+#pragma unroll
+    for (int j = 0; j < 32; ++j) bias[j] = 0.0f;
+  } else if (col + 32 <= p.n && (reinterpret_cast<std::uintptr_t>(p.bias + col) & 15u) == 0) {
     const float4* b4 = reinterpret_cast<const float4*>(p.bias + col);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
@@ -403,7 +414,7 @@ __device__ __forceinline__ void epilogue_values(const TcParams& p, int row, int 
     }
   } else {
 #pragma unroll
-    for (int j = 0; j < 32; ++j) bias[j] = (p.bias != nullptr && col + j < p.n) ? __ldg(p.bias + col + j) : 0.0f;
+    for (int j = 0; j < 32; ++j) bias[j] = col + j < p.n ? __ldg(p.bias + col + j) : 0.0f;
   }
 #pragma unroll
   for (int j = 0; j < 32; ++j) {
@@ -562,11 +573,14 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
           const float4 b0 = bias_s != nullptr ? src[2 * q] : __ldg(src + 2 * q);
           const float4 b1 = bias_s != nullptr ? src[2 * q + 1] : __ldg(src + 2 * q + 1);
           b[0] = b0.x, b[1] = b0.y, b[2] = b0.z, b[3] = b0.w, b[4] = b1.x, b[5] = b1.y, b[6] = b1.z, b[7] = b1.w;
+        } else if (p.bias == nullptr) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) b[j] = 0.0f;
         } else {
 #pragma unroll
           for (int j = 0; j < 8; ++j) {
             const int c = col + 8 * q + j;
-            b[j] = (p.bias != nullptr && c < p.n) ? __ldg(p.bias + c) : 0.0f;
+            b[j] = c < p.n ? __ldg(p.bias + c) : 0.0f;
           }
         }
         std::uint32_t packed[4];
