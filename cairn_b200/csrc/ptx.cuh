@@ -4,7 +4,9 @@
 // returns false, so a kernel whose partner never arrives ends with an error status instead of hanging the GPU.
 #pragma once
 #include <cstdint>
+#include <cstring>
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 namespace cb {
@@ -23,6 +25,14 @@ enum Fault : std::uint32_t {
   FAULT_WATCHDOG = 1u << 6,     // the watchdog self-test's wait (on a barrier nothing completes) ran out
   FAULT_WAIT_MASK = 1u << 7,    // an epilogue warp waited for its ReLU-gradient mask tile's TMA load
 };
+
+// Two floats rounded to bf16 (to nearest even) and packed, `lo` at the lower address.
+__device__ __forceinline__ std::uint32_t bf16x2_bits(float lo, float hi) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  std::uint32_t u;
+  std::memcpy(&u, &h, 4);
+  return u;
+}
 
 // A flag another CTA raises: read with acquire ordering at GPU scope, raised with release ordering.
 __device__ __forceinline__ std::uint32_t ld_acquire_gpu(const std::uint32_t* p) {

@@ -286,13 +286,6 @@ __device__ __forceinline__ double block_sum_f64(double v, double* shared) {
   return t;
 }
 
-__device__ __forceinline__ std::uint32_t bf16x2_bits(float lo, float hi) {
-  const __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);  // lo at the lower address
-  std::uint32_t u;
-  std::memcpy(&u, &h, 4);
-  return u;
-}
-
 // VEC: y and t start on 16 bytes and dy on 8, so four elements move per float4 load and 8-byte store, UNROLL vectors
 // of each operand in flight per thread (the saxpy kernel's shape); the last n % 4 elements run in block 0.
 template <bool VEC>
