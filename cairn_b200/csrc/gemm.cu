@@ -477,6 +477,34 @@ __device__ __forceinline__ void store_chunk_bf16_tma(const TcParams& p, int row0
   }
 }
 
+// An f32 chunk through the output's tensor map, a 16-column half (32 rows of 64 bytes, swizzled as above) at a time.
+// The accumulate form (C += A B, p.tma_store == 2) hands each half to a TMA reduce-add: L2 adds it to C element by
+// element, each sum rounded once to nearest, as old + acc rounded in the epilogue would be; one tile owns each
+// element, so each is added once. Like store_chunk_bf16_tma, the drain runs it in a loop of its own.
+__device__ __forceinline__ void store_chunk_f32_tma(const TcParams& p, int row0, int col, const std::uint32_t (&r)[32],
+                                                    std::uint8_t* stage, int lane, const CUtensorMap* tm_c) {
+  std::uint8_t* mine = stage + lane * 64;
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    if (lane == 0) bulk_wait_read();
+    __syncwarp();
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      *reinterpret_cast<float4*>(mine + 16 * (q ^ ((lane >> 1) & 3))) =
+          make_float4(__uint_as_float(r[16 * half + 4 * q]), __uint_as_float(r[16 * half + 4 * q + 1]),
+                      __uint_as_float(r[16 * half + 4 * q + 2]), __uint_as_float(r[16 * half + 4 * q + 3]));
+    fence_proxy_async_shared();
+    __syncwarp();
+    if (lane == 0) {
+      if (p.tma_store == 2)
+        tma_reduce_add_2d(tm_c, smem_u32(stage), col + 16 * half, row0);
+      else
+        tma_store_2d(tm_c, smem_u32(stage), col + 16 * half, row0);
+      bulk_commit();
+    }
+  }
+}
+
 template <bool LOADS, bool MASKED>
 __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, int col, const std::uint32_t (&r)[32],
                                                    std::uint8_t* stage, int lane, const float* bias_s,
@@ -521,29 +549,7 @@ __device__ __forceinline__ void store_chunk_staged(const TcParams& p, int row0, 
       return;
     }
     if ((p.out_kind == OUT_STORE_F32 || p.out_kind == OUT_ACC_F32) && p.tma_store) {
-      // f32 outputs the same way, a 16-column half (32 rows of 64 bytes) at a time. The accumulate form (C += A B)
-      // hands the half to a TMA reduce-add: L2 adds it to C element by element, each sum rounded once to nearest,
-      // as old + acc rounded in the epilogue would be; one tile owns each element, so each is added once.
-      std::uint8_t* mine = stage + lane * 64;
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        if (lane == 0) bulk_wait_read();
-        __syncwarp();
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          *reinterpret_cast<float4*>(mine + 16 * (q ^ ((lane >> 1) & 3))) =
-              make_float4(__uint_as_float(r[16 * half + 4 * q]), __uint_as_float(r[16 * half + 4 * q + 1]),
-                          __uint_as_float(r[16 * half + 4 * q + 2]), __uint_as_float(r[16 * half + 4 * q + 3]));
-        fence_proxy_async_shared();
-        __syncwarp();
-        if (lane == 0) {
-          if (p.tma_store == 2)
-            tma_reduce_add_2d(tm_c, smem_u32(stage), col + 16 * half, row0);
-          else
-            tma_store_2d(tm_c, smem_u32(stage), col + 16 * half, row0);
-          bulk_commit();
-        }
-      }
+      store_chunk_f32_tma(p, row0, col, r, stage, lane, tm_c);
       return;
     }
   }
@@ -1026,8 +1032,9 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       } else {
         // Otherwise the drain is double-buffered: a TMEM load takes several hundred cycles to reach the registers,
         // so each chunk's load is issued before the chunk ahead of it is written out. The accumulator goes back to
-        // the MMA issuer once the last chunk's load has landed. CHUNKS is even (8 for G = 2, 4 for G = 1). Plain
-        // bf16 outputs by TMA store run the loop with their own compact chunk body.
+        // the MMA issuer once the last chunk's load has landed. CHUNKS is even (8 for G = 2, 4 for G = 1). Outputs
+        // that leave by plain TMA stores (bf16) or TMA stores and reduce-adds (f32) run the loop with their own
+        // compact chunk bodies.
         auto drain_chunks = [&](auto&& put) {
           std::uint32_t ra[32], rb[32];
           tmem_ld_32x32b_x32(t_row + col0, ra);
@@ -1051,6 +1058,10 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
           drain_chunks([&](int ci, const std::uint32_t(&r)[32]) {
             store_chunk_bf16_tma(p, row0, c_first + ci * 32, r, stage, lane,
                                  bias_s != nullptr ? bias_s + ci * 32 : nullptr, &tm_c);
+          });
+        } else if (p.out_kind != OUT_BF16 && p.tma_store != 0 && !split) {
+          drain_chunks([&](int ci, const std::uint32_t(&r)[32]) {
+            store_chunk_f32_tma(p, row0, c_first + ci * 32, r, stage, lane, &tm_c);
           });
         } else {
           drain_chunks(emit);
