@@ -150,7 +150,8 @@ class ClockSampler:
             inside = [s for _, s in nearest]
             note = "timed region shorter than the 50 ms sampling period: nearest samples of the same run"
         if not inside:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+            why = "nvidia-smi unavailable" if self.proc is None else "no nvidia-smi samples in or near the timed region"
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": why}
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for s in inside for i in range(4) if s[2 + i].lower().startswith("active")})
         out = {"sm_mhz": statistics.median(float(s[0]) for s in inside), "sm_max_mhz": float(inside[0][1]),
@@ -437,13 +438,15 @@ class Stream:
         return self.dist.world * chunk * self.bytes / (ms * 1e-3) / 1e9, h2d, d2h
 
 
-EMITTED = ROOT / "tests" / "dropin" / "_build" / "libemitted.so"
+EMITTED = ROOT / "tests" / "dropin" / "_build" / "libhotpath.so"
+SCAN_PROBE = ROOT / "tests" / "dropin" / "_build" / "libscanprobe.so"
 
 
 class Scan:
-    """The drop-in machine's device scan over n = 2^30 u32 (add_wrap), through an emitted-style CAIRN library built
-    over include/cairn_b200/runtime (cq_wscan: the reference's scan_into, which scans into its arena and copies to
-    out), and the machine's scan kernel alone (b200_scan_u32) for the roofline. 8 algorithmic bytes per element."""
+    """The drop-in machine's device scan over n = 2^30 u32 (add_wrap), through the compiler-emitted CAIRN library
+    built over include/cairn_b200/runtime (cf_wscan: `scan add_wrap out parallel i in n yield x[i]`, the reference's
+    scan_into, which scans into its arena and copies to out, then waits for its stream), and the machine's scan kernel
+    alone (tests/dropin/scan_probe.cu's b200_scan_u32) for the roofline. 8 algorithmic bytes per element."""
 
     def __init__(self, dist: Dist, log2n: int = 30):
         import torch
@@ -456,33 +459,36 @@ class Scan:
         self.out = torch.empty_like(self.x)
         lib_handle()  # the program links libcairn_b200.so: load it from the tree first
         h = C.CDLL(str(EMITTED))
-        h.cq_wscan.restype, h.cq_wscan.argtypes = None, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p]
-        h.b200_scan_u32_scratch.restype, h.b200_scan_u32_scratch.argtypes = C.c_size_t, [C.c_size_t]
-        h.b200_scan_u32.restype = None
-        h.b200_scan_u32.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p]
-        self.h = h
-        self.temp = torch.empty(h.b200_scan_u32_scratch(self.n), dtype=torch.uint8, device=dev)
+        h.cf_wscan.restype, h.cf_wscan.argtypes = None, [C.c_size_t, C.c_void_p, C.c_void_p]
+        h.cairn_hotpath_device_stream.restype, h.cairn_hotpath_device_stream.argtypes = None, [C.c_void_p]
+        probe = C.CDLL(str(SCAN_PROBE))
+        probe.b200_scan_u32_scratch.restype, probe.b200_scan_u32_scratch.argtypes = C.c_size_t, [C.c_size_t]
+        probe.b200_scan_u32.restype = None
+        probe.b200_scan_u32.argtypes = [C.c_void_p, C.c_size_t, C.c_void_p, C.c_void_p, C.c_void_p]
+        self.h, self.probe = h, probe
+        self.temp = torch.empty(probe.b200_scan_u32_scratch(self.n), dtype=torch.uint8, device=dev)
         self.stream = torch.cuda.current_stream(dev)
+        h.cairn_hotpath_device_stream(self.stream.cuda_stream)  # the program's work on the bench's stream
         self.bytes = 8
         self.scaling = "weak"
 
     def launch(self, i: int):
-        self.h.cq_wscan(self.stream.cuda_stream, self.n, self.out.data_ptr(), self.x.data_ptr())
+        self.h.cf_wscan(self.n, self.out.data_ptr(), self.x.data_ptr())
 
     def kernel_alone(self, i: int):
-        self.h.b200_scan_u32(self.stream.cuda_stream, self.n, self.out.data_ptr(), self.x.data_ptr(),
-                             self.temp.data_ptr())
+        self.probe.b200_scan_u32(self.stream.cuda_stream, self.n, self.out.data_ptr(), self.x.data_ptr(),
+                                 self.temp.data_ptr())
 
     def e2e(self, steps: int, warmup: int):
         torch = self.torch
         chunk = min(self.n, 1 << 26)  # the e2e sample: 2^26 elements from pinned host memory
         x_h = self.x[:chunk].cpu().pin_memory()
         o_h = torch.empty(chunk, dtype=torch.int32).pin_memory()
-        x_d, o_d, st = self.x[:chunk], self.out[:chunk], self.stream.cuda_stream
+        x_d, o_d = self.x[:chunk], self.out[:chunk]
 
         def step(i):
             x_d.copy_(x_h, non_blocking=True)
-            self.h.cq_wscan(st, chunk, o_d.data_ptr(), x_d.data_ptr())
+            self.h.cf_wscan(chunk, o_d.data_ptr(), x_d.data_ptr())
             o_h.copy_(o_d, non_blocking=True)
 
         ms, _, _, _ = time_steps(self.dist, self.stream, step, steps, warmup, per_launch=False)
@@ -554,32 +560,41 @@ def cpu_mlp_sample(budget_s: float):
 
 
 # ---------------------------------------------------------------------------------------------------------------------
-REF_DEVICE = ROOT / "baseline" / "_ref" / "libemitted_ref.so"
+REF_DEVICE = ROOT / "baseline" / "_ref" / "libhotpath_ref.so"
+
+# The compiler-emitted entries of tests/dropin/programs/hotpath.cairn timed on each machine, with their C types and
+# algorithmic bytes per element (regions and collectors) or None (the multiply).
+MACHINE_ENTRIES = {
+    "cq_saxpy": (None, ["p", "z", "p", "p", "p", "f"], 12), "cq_saxpy4": (None, ["p", "z", "p", "p", "p", "f"], 12),
+    "cq_blur": (None, ["p", "z", "p", "p"], 8), "cf_dsum": ("f", ["z", "p"], 4), "cf_usum": ("u64", ["z", "p"], 8),
+    "cf_wscan": (None, ["z", "p", "p"], 8), "cq_gemm": (None, ["p", "z", "z", "z", "z", "p", "z", "p", "z", "p"], None),
+    "cairn_hotpath_device_stream": (None, ["p"], None),
+}
 
 
-def reference_device_measure(args) -> dict:
-    """The reference's own CUDA path on this GPU (baseline/_ref/libemitted_ref.so: tests/dropin/emitted_program.cu
-    built over the reference's runtime headers alone, for sm_100a): its WMMA multiply (cr::tensor::launch, 64 x 64
-    tiles), its lane kernel (cr::gpu::run), its CUB collectors (reduce_on) and its scan_into over CUB. Runs in a
-    process of its own, after this project's timed region; inputs are resident in HBM. Enqueued entries (cq_) are
-    timed with CUDA events on the stream they are given; the cf_ sums, which return their total to the host, by the
-    host clock around the call (each includes the total's copy back and the wait, as the reference's entry does)."""
+def machine_measure(args) -> dict:
+    """One machine's timings of the compiler-emitted program (tests/dropin/programs/hotpath.cairn): `args.machine` is
+    tests/dropin/_build/libhotpath.so (this project's B200 machine under the drop-in headers) or
+    baseline/_ref/libhotpath_ref.so (the same emitted source over the reference's own headers: its lane kernels, CUB
+    collectors and WMMA multiply). Runs in a process of its own (two builds of one program would share template
+    symbols). Inputs resident in HBM, n = 2^log2n; every entry runs on the bench's stream (bound with
+    cairn_hotpath_device_stream for the cf_ ones), each timed over 10 calls with CUDA events after 2 untimed ones.
+    cf_ entries wait for their stream and copy their total back, on either machine alike."""
     import torch
 
-    h = C.CDLL(str(REF_DEVICE))
-    z, p = C.c_size_t, C.c_void_p
-    sig = {"cq_gemm": (None, [p, z, z, z, z, p, z, p, z, p]), "cq_saxpy": (None, [p, z, p, p, p, C.c_float]),
-           "cf_dsum": (C.c_float, [z, p]), "cf_usum": (C.c_uint64, [z, p]), "cq_wscan": (None, [p, z, p, p])}
-    for name, (res, argt) in sig.items():
+    types = {"p": C.c_void_p, "z": C.c_size_t, "f": C.c_float, "u64": C.c_uint64, None: None}
+    h = C.CDLL(str(args.machine))
+    for name, (res, argt, _) in MACHINE_ENTRIES.items():
         f = getattr(h, name)
-        f.restype, f.argtypes = res, argt
+        f.restype, f.argtypes = types[res], [types[a] for a in argt]
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
+    h.cairn_hotpath_device_stream(stream.cuda_stream)
+    st = stream.cuda_stream
     g = torch.Generator(device=dev).manual_seed(0)
-    w = args.workload
 
-    def events(fn, steps: int, warmup: int) -> float:
+    def events(fn, steps: int = 10, warmup: int = 2) -> float:
         for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
@@ -591,66 +606,77 @@ def reference_device_measure(args) -> dict:
         torch.cuda.synchronize()
         return e0.elapsed_time(e1) / steps
 
-    def clock(fn, steps: int, warmup: int) -> float:
-        for _ in range(warmup):
-            fn()
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(steps):
-            fn()
-        return (time.perf_counter() - t0) * 1e3 / steps
-
-    if w in ("gemm", "gemm5"):
-        m, n, k = (4096, 4096, 4096) if w == "gemm" else (65536, 8192, 8192)
-        a = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
-        b = (torch.randn(k, n, device=dev, generator=g) * (1.0 if w == "gemm" else 0.02)).to(torch.bfloat16)
-        c = torch.zeros(m, n, device=dev)
-        ms = events(lambda: h.cq_gemm(stream.cuda_stream, m, n, k, m * n, c.data_ptr(), m * k, a.data_ptr(), k * n,
-                                      b.data_ptr()), 3 if w == "gemm5" else 10, 1)
-        return {"value": 2.0 * m * n * k / (ms * 1e-3) / 1e12, "unit": "TFLOP/s", "ms": ms,
-                "what": "the reference's mma_unordered (cr::tensor::launch: WMMA 16x16x16, 64 x 64 tiles) on "
-                        f"{m}x{n}x{k} bf16 with f32 C += A B (it has no fused bias/ReLU epilogue)"}
-    if w == "mlp":
-        return {"unavailable": "the reference's derive-grad backward runs on the host only, and its device multiply "
-                               "takes no transposed operand"}
+    out: dict = {"n": 1 << args.log2n}
     n = 1 << args.log2n
-    if w == "saxpy":
-        x = torch.rand(n, device=dev, generator=g) * 2 - 1
-        y = torch.rand(n, device=dev, generator=g) * 2 - 1
-        out = torch.empty_like(x)
-        ms = events(lambda: h.cq_saxpy(stream.cuda_stream, n, out.data_ptr(), x.data_ptr(), y.data_ptr(), 2.5), 10, 2)
-        what, per = "cr::gpu::run of out[i] = a x[i] + y[i] (the reference's lane kernel)", 12
-    elif w == "sum_f32":
-        x = torch.rand(n, device=dev, generator=g) * 2 - 1
-        ms = clock(lambda: h.cf_dsum(n, x.data_ptr()), 10, 2)
-        what, per = "reduce_on<float> over CUB's DeviceReduce (total copied back and awaited)", 4
-    elif w == "sum_u64":
-        u = torch.arange(n, device=dev, dtype=torch.int64)
-        ms = clock(lambda: h.cf_usum(n, u.data_ptr()), 10, 2)
-        what, per = "reduce_on<Sum<u64>> over CUB's DeviceReduce (total copied back and awaited)", 8
-    else:  # scan
-        x = torch.randint(-2**31, 2**31 - 1, (n,), device=dev, dtype=torch.int32, generator=g)
-        out = torch.empty_like(x)
-        ms = events(lambda: h.cq_wscan(stream.cuda_stream, n, out.data_ptr(), x.data_ptr()), 10, 2)
-        what, per = "scan_into over CUB's DeviceScan (the reference context's scan, then its copy pass)", 8
-    return {"value": n * per / (ms * 1e-3) / 1e9, "unit": "GB/s", "ms": ms, "what": what}
+    x = torch.rand(n, device=dev, generator=g) * 2 - 1
+    y = torch.rand(n, device=dev, generator=g) * 2 - 1
+    o = torch.empty_like(x)
+    runs = {
+        "saxpy": lambda: h.cq_saxpy(st, n, o.data_ptr(), x.data_ptr(), y.data_ptr(), 2.5),
+        "saxpy4": lambda: h.cq_saxpy4(st, n, o.data_ptr(), x.data_ptr(), y.data_ptr(), 2.5),
+        "blur": lambda: h.cq_blur(st, n, o.data_ptr(), x.data_ptr()),
+        "dsum": lambda: h.cf_dsum(n, x.data_ptr()),
+        "wscan": lambda: h.cf_wscan(n, o.data_ptr(), x.data_ptr()),
+    }
+    per = {"saxpy": 12, "saxpy4": 12, "blur": 8, "dsum": 4, "wscan": 8}
+    for name, fn in runs.items():
+        ms = events(fn)
+        out[name] = {"GB/s": n * per[name] / (ms * 1e-3) / 1e9, "ms": ms}
+    del y
+    u = torch.arange(n, device=dev, dtype=torch.int64)
+    ms = events(lambda: h.cf_usum(n, u.data_ptr()))
+    out["usum"] = {"GB/s": n * 8 / (ms * 1e-3) / 1e9, "ms": ms}
+    del u, x, o
+    if args.workload in ("gemm", "gemm5"):
+        m, nn, k = (4096, 4096, 4096) if args.workload == "gemm" else (65536, 8192, 8192)
+        a = torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+        b = (torch.randn(k, nn, device=dev, generator=g) * (1.0 if args.workload == "gemm" else 0.02)).to(torch.bfloat16)
+        c = torch.zeros(m, nn, device=dev)
+        ms = events(lambda: h.cq_gemm(st, m, nn, k, m * nn, c.data_ptr(), m * k, a.data_ptr(), k * nn, b.data_ptr()),
+                    3 if args.workload == "gemm5" else 10, 1)
+        out["gemm"] = {"TFLOP/s": 2.0 * m * nn * k / (ms * 1e-3) / 1e12, "ms": ms, "shape": [m, nn, k]}
+    h.cairn_hotpath_device_stream(None)
+    return out
 
 
-def reference_device_leg(args) -> dict | None:
-    """Runs reference_device_measure in a fresh process (python bench.py --reference-device ...) and returns its
-    result, or a note saying why there is none."""
-    if not REF_DEVICE.exists():
-        return {"unavailable": "baseline/_ref/libemitted_ref.so is not built (it needs the CAIRN reference's headers)"}
-    cmd = [sys.executable, str(Path(__file__).resolve()), "--reference-device", "--workload", args.workload,
+def machine_leg(args, lib: Path) -> dict:
+    """machine_measure in a fresh process (python bench.py --machine-measure LIB ...), or why there is none."""
+    if not lib.exists():
+        return {"unavailable": f"{lib.relative_to(ROOT)} is not built (it needs the CAIRN reference's compiler)"}
+    cmd = [sys.executable, str(Path(__file__).resolve()), "--machine-measure", str(lib), "--workload", args.workload,
            "--log2n", str(args.log2n)]
     try:
-        done = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+        done = subprocess.run(cmd, capture_output=True, text=True, timeout=900)
     except subprocess.TimeoutExpired:
-        return {"unavailable": "the reference's device path did not finish within 600 s"}
+        return {"unavailable": f"{lib.name} did not finish within 900 s"}
     lines = [ln for ln in done.stdout.splitlines() if ln.startswith("{")]
     if done.returncode != 0 or not lines:
-        return {"unavailable": f"the reference's device path exited {done.returncode}: {done.stderr[-300:]}"}
+        return {"unavailable": f"{lib.name} exited {done.returncode}: {done.stderr[-300:]}"}
     return json.loads(lines[-1])
+
+
+def dropin_report(args) -> tuple[dict, dict | None]:
+    """The compiler-emitted program on both machines, and the reference machine's figure for this workload (the
+    reference's own CUDA path on this GPU: its WMMA multiply, lane kernel, CUB collectors), or None."""
+    ours, ref = machine_leg(args, EMITTED), machine_leg(args, REF_DEVICE)
+    report = {"program": "tests/dropin/programs/hotpath.cairn, emitted by the reference's compiler; the same "
+                         "emitted C++ built over the drop-in headers (b200) and over the reference's own (reference)",
+              "b200": ours, "reference": ref}
+    if "unavailable" in ref:
+        return report, ref
+    key = {"gemm": "gemm", "gemm5": "gemm", "saxpy": "saxpy", "sum_f32": "dsum", "sum_u64": "usum",
+           "scan": "wscan"}.get(args.workload)
+    if key is None or key not in ref:
+        return report, {"unavailable": "the reference's derive-grad backward runs on the host only, and its device "
+                                       "multiply takes no transposed operand"}
+    unit = "TFLOP/s" if key == "gemm" else "GB/s"
+    what = {"gemm": "the reference's mma_unordered (cr::tensor::launch: WMMA 16x16x16, 64 x 64 tiles), f32 C += A B "
+                    "(it has no fused bias/ReLU epilogue)",
+            "saxpy": "cr::gpu::run of out[i] = a x[i] + y[i] (the reference's lane kernel)",
+            "dsum": "reduce_on<float> over CUB's DeviceReduce (total copied back and awaited)",
+            "usum": "reduce_on<Sum<u64>> over CUB's DeviceReduce (total copied back and awaited)",
+            "wscan": "scan_into over CUB's DeviceScan (the reference context's scan, then its copy pass)"}[key]
+    return report, {"value": ref[key][unit], "unit": unit, "ms": ref[key]["ms"], "what": what}
 
 
 def reference_arm(args, dist: Dist) -> None:
@@ -726,11 +752,12 @@ def main() -> None:
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU-baseline leg")
     ap.add_argument("--log2n", type=int, default=30, help="saxpy/sum size 2^log2n (BASELINE: 30; smaller for ncu)")
     ap.add_argument("--no-reference-device", action="store_true",
-                    help="skip the reference-on-B200 leg (the reference's own CUDA path, timed in a subprocess)")
-    ap.add_argument("--reference-device", action="store_true", help=argparse.SUPPRESS)  # that subprocess
+                    help="skip the drop-in legs (the emitted program on both machines, timed in subprocesses)")
+    ap.add_argument("--machine-measure", default=None, help=argparse.SUPPRESS)  # that subprocess
     args = ap.parse_args()
-    if args.reference_device:
-        print(json.dumps(reference_device_measure(args)), flush=True)
+    if args.machine_measure:
+        args.machine = args.machine_measure
+        print(json.dumps(machine_measure(args)), flush=True)
         return
     defaults = {"gemm": (2000, 50), "gemm5": (50, 5), "mlp": (40, 5), "saxpy": (100, 5), "sum_f32": (200, 5),
                 "sum_u64": (100, 5), "scan": (50, 5)}
@@ -747,23 +774,24 @@ def main() -> None:
         return
     import torch
 
+    sampler = ClockSampler(dist.local)  # started before the set-up, so it is sampling when the timed region begins
     if args.workload.startswith("gemm"):
         wl = Gemm(dist, args.workload == "gemm5")
     elif args.workload == "mlp":
         wl = Mlp(dist)
     elif args.workload == "scan":
         if not EMITTED.exists():
+            sampler.stop()
             if dist.rank == 0:
                 print(json.dumps({"metric": BASELINE_METRIC, "workload": "scan", "unavailable":
-                                  "tests/dropin/_build/libemitted.so is not built (it needs the CAIRN reference's "
-                                  "runtime headers, present where __graft_entry__.build() ran)"}), flush=True)
+                                  "tests/dropin/_build/libhotpath.so is not built (it needs the CAIRN reference's "
+                                  "compiler, present where __graft_entry__.build() ran)"}), flush=True)
             dist.close()
             return
         wl = Scan(dist, args.log2n)
     else:
         wl = Stream(dist, args.workload, args.log2n)
     peaks, peak_source = measured_peaks()
-    sampler = ClockSampler(dist.local)
     ms, launch_ms, t0, t1 = time_steps(dist, wl.stream, wl.launch, args.steps, args.warmup)
     clocks = sampler.window(t0, t1)
     sampler.stop()
@@ -805,9 +833,9 @@ def main() -> None:
             v, cores, kind, sample = cpu_stream_sample(args.workload, 12.0)
         cpu = {"value": v, "unit": unit, "cores": cores, "kind": kind, "sample": sample}
 
-    refdev = None
+    refdev = dropin = None
     if dist.rank == 0 and dist.world == 1 and not args.no_reference_device:
-        refdev = reference_device_leg(args)
+        dropin, refdev = dropin_report(args)
 
     launches = args.steps * (7 if isinstance(wl, Mlp) else 2 if isinstance(wl, Scan) else
                              1 if isinstance(wl, Gemm) or args.workload != "sum_f32" or dist.world == 1 else 2)
@@ -824,6 +852,7 @@ def main() -> None:
                      "traffic": traffic},
         "cpu_baseline": cpu,
         "reference_on_b200": refdev,
+        "dropin_machines": dropin,
         "clocks": clocks,
         "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "gpu_launches": launches,

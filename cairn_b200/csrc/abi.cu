@@ -366,8 +366,10 @@ int cairn_b200_saxpy_f32(void* stream, size_t n, float* out, const float* x, con
 
 static int sum_f32_common(void* stream, size_t n, const float* x, float* out32, double* out64) {
   if (!view_ok(x, n, 4, 4)) return CAIRN_B200_ERR_VIEW;
-  if (out32 && (!view_ok(out32, 1, 4, 4) || overlaps(out32, 4, x, n * 4))) return CAIRN_B200_ERR_VIEW;
-  if (out64 && (!view_ok(out64, 3, 8, 8) || overlaps(out64, 24, x, n * 4))) return CAIRN_B200_ERR_VIEW;
+  if (out32 && !view_ok(out32, 1, 4, 4)) return CAIRN_B200_ERR_VIEW;
+  if (out64 && !view_ok(out64, 3, 8, 8)) return CAIRN_B200_ERR_VIEW;
+  if ((out32 && overlaps(out32, 4, x, n * 4)) || (out64 && overlaps(out64, 24, x, n * 4)))
+    return CAIRN_B200_ERR_OVERLAP;
   int status;
   const Device* d = current(&status);
   if (!d) return status;

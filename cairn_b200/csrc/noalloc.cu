@@ -42,7 +42,9 @@ struct StaticScratch {
 std::mutex g_static_mutex;
 StaticScratch g_static[MAX_DEVICES];
 
-// Once per device, with the device current: its SM count and the array's device address.
+// Once per device, with the device current: its SM count and the array's device address. Only a definite answer
+// is kept (the address, or a device that is not an sm_100 part); a CUDA call that failed, for example because the
+// first call came during a stream capture, leaves the device unresolved, and the next call asks again.
 const StaticScratch* static_scratch(int* status) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= MAX_DEVICES) {
@@ -52,17 +54,26 @@ const StaticScratch* static_scratch(int* status) {
   std::lock_guard<std::mutex> hold(g_static_mutex);
   StaticScratch& s = g_static[dev];
   if (!s.ready) {
-    cudaDeviceProp prop{};
-    if (cudaGetDeviceProperties(&prop, dev) != cudaSuccess) {
-      s.status = CAIRN_B200_ERR_CUDA;
-    } else if (prop.major != 10) {
+    int major = 0, sms = 0;
+    if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+      cudaGetLastError();
+      *status = CAIRN_B200_ERR_CUDA;
+      return nullptr;
+    }
+    if (major != 10) {
       s.status = CAIRN_B200_ERR_DEVICE;
     } else {
-      s.sms = prop.multiProcessorCount;
       void* p = nullptr;
       const cudaError_t e = cudaGetSymbolAddress(&p, g_static_scratch);
-      if (e != cudaSuccess || p == nullptr) s.status = CAIRN_B200_ERR_CUDA;
-      else s.ptr = static_cast<unsigned char*>(p);
+      if (e != cudaSuccess || p == nullptr) {
+        cudaGetLastError();
+        *status = CAIRN_B200_ERR_CUDA;
+        return nullptr;
+      }
+      s.sms = sms;
+      s.ptr = static_cast<unsigned char*>(p);
+      s.status = CAIRN_B200_OK;
     }
     s.ready = true;
   }

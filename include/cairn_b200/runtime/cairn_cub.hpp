@@ -3,11 +3,13 @@
 // :7-36), and the older synchronous forms. Nothing here uses CUB (runtime/cairn_cub.hpp:14-25 calls DeviceReduce and
 // DeviceScan).
 //
-// B200::reduce: one launch of a device-sized persistent grid, each thread folding a grid-strided run of value(i) in
-// registers, a shared-memory tree per block, one partial per block in the scratch the context lends, and the last
-// block to finish (an atomic ticket) folding the partials and storing the total. The order of the folds is fixed by
-// n and the device; the operator must be associative and commutative, which every operator a device `reduce` admits
-// is (+ over the checked Sum, add_wrap, *, min, max, &, |, ^).
+// B200::reduce: one launch of a device-sized persistent grid. Each thread loads eight values of a tile (four for
+// values wider than 8 bytes) before folding them into as many accumulators, so eight loads per thread are in flight;
+// the accumulators fold pairwise, each warp folds by shuffles, the block's eight warp totals fold in warp 0, one
+// partial per block goes to the scratch the context lends, and the last block to finish (an atomic ticket) folds
+// the partials and stores the total. The order of the folds is fixed by n and the device; the operator must be
+// associative and commutative, which every operator a device `reduce` admits is (+ over the checked Sum, add_wrap,
+// *, min, max, &, |, ^).
 //
 // B200::inclusive_scan and exclusive_sum: one pass over the input with decoupled look-back (Merrill and Garland,
 // "Single-pass Parallel Prefix Scan with Decoupled Look-back", NVIDIA technical report NVR-2016-002). Each block
@@ -29,13 +31,12 @@ namespace cr::gpu {
 namespace b200 {
 
 constexpr unsigned FOLD_THREADS = 256;
+constexpr unsigned FOLD_WARPS = FOLD_THREADS / 32;
+constexpr unsigned FOLD_BLOCKS_PER_SM = 8;  // 2048 threads: every thread slot of an SM
+// Independent accumulators per thread, which is also how many of a thread's loads are in flight at once: eight for
+// values of up to 8 bytes (eight 128-byte warp loads of 4-byte values), four for larger ones.
+template<class T> constexpr unsigned fold_ways() noexcept { return sizeof(T) <= 8 ? 8u : 4u; }
 
-// Blocks of a reduction over n values on the current device: no more than the work needs, four per SM at most.
-inline unsigned fold_grid(std::size_t n) noexcept {
-  const std::size_t needed = (n + FOLD_THREADS - 1) / FOLD_THREADS;
-  const std::size_t most = std::size_t(sm_count()) * 4;
-  return unsigned(needed < most ? (needed ? needed : 1) : most);
-}
 inline std::size_t fold_partials_bytes(unsigned grid, std::size_t t_size) noexcept {
   return (std::size_t(grid) * t_size + 255) / 256 * 256;
 }
@@ -58,32 +59,73 @@ template<class T> __device__ inline T read_fresh(const T* p) {
   return v;
 }
 
-// The block's fold of one value per thread, in thread order pairs; thread 0 holds it on return.
-template<class T, class Fold> __device__ inline T fold_block(T v, Fold& fold, T* shared) {
-  shared[threadIdx.x] = v;
-  __syncthreads();
-  for(unsigned w = FOLD_THREADS / 2; w; w >>= 1) {
-    if(threadIdx.x < w) shared[threadIdx.x] = fold(shared[threadIdx.x], shared[threadIdx.x + w]);
-    __syncthreads();
-  }
-  const T r = shared[0];
-  __syncthreads();
+// The value `down` lanes above this one in the warp, moved a 32-bit word at a time (any trivially copyable T).
+template<class T> __device__ inline T from_lane_above(const T& v, unsigned down) {
+  constexpr unsigned WORDS = (sizeof(T) + 3) / 4;
+  unsigned w[WORDS] = {};
+  std::memcpy(w, &v, sizeof(T));
+#pragma unroll
+  for(unsigned i = 0; i < WORDS; ++i) w[i] = __shfl_down_sync(0xffffffffu, w[i], down);
+  T r;
+  std::memcpy(&r, w, sizeof(T));
   return r;
 }
 
+// A warp's fold of one value per lane: five shuffle steps, lane 0 holds the result.
+template<class T, class Fold> __device__ inline T fold_warp(T v, Fold& fold) {
+#pragma unroll
+  for(unsigned down = 16; down; down >>= 1) v = fold(v, from_lane_above(v, down));
+  return v;
+}
+
+// A block's fold of one value per thread: each warp by shuffles, then the eight warp totals by warp 0. Thread 0
+// holds the result; every thread of the block must call it.
+template<class T, class Fold> __device__ inline T fold_block(T v, Fold& fold, T identity, T* warp_totals) {
+  v = fold_warp(v, fold);
+  const unsigned lane = threadIdx.x % 32, warp = threadIdx.x / 32;
+  if(lane == 0) warp_totals[warp] = v;
+  __syncthreads();
+  T r = identity;
+  if(warp == 0) r = fold_warp(lane < FOLD_WARPS ? warp_totals[lane] : identity, fold);
+  __syncthreads();  // warp_totals may be written again
+  return r;
+}
+
+// The reduction: a persistent grid over tiles of fold_ways<T>() * FOLD_THREADS consecutive values, each thread
+// loading its fold_ways values of a tile (coalesced: step k of a warp reads 32 consecutive values) before it folds
+// them into as many accumulators; the accumulators fold pairwise, the block folds by shuffles, one partial per block
+// lands in the scratch, and the last block to arrive (an atomic ticket) folds the partials and stores the total.
+// The order is fixed by n and the grid; every operator a device `reduce` admits is associative and commutative.
 template<class T, class In, class Out, class Fold>
 __global__ void __launch_bounds__(FOLD_THREADS)
     fold_kernel(In in, Out out, std::size_t n, Fold fold, T identity, T* partials, unsigned* ticket) {
-  static_assert(alignof(T) <= 16, "a fold value fits the shared tree's alignment");
-  __shared__ __align__(16) unsigned char raw[FOLD_THREADS * sizeof(T)];
+  static_assert(alignof(T) <= 16, "a fold value fits the shared totals' alignment");
+  constexpr unsigned K = fold_ways<T>();
+  __shared__ __align__(16) unsigned char raw[FOLD_WARPS * sizeof(T)];
   __shared__ bool last;
-  T* shared = reinterpret_cast<T*>(raw);
-  const std::size_t stride = std::size_t(gridDim.x) * FOLD_THREADS;
-  T acc = identity;
-  for(std::size_t i = blockIdx.x * std::size_t(FOLD_THREADS) + threadIdx.x; i < n; i += stride) acc = fold(acc, in[i]);
-  acc = fold_block(acc, fold, shared);
+  T* warp_totals = reinterpret_cast<T*>(raw);
+  T acc[K];
+#pragma unroll
+  for(unsigned k = 0; k < K; ++k) acc[k] = identity;
+  const std::size_t width = std::size_t(K) * FOLD_THREADS, whole = n / width;
+  std::size_t tile = blockIdx.x;
+  for(; tile < whole; tile += gridDim.x) {
+    const std::size_t first = tile * width + threadIdx.x;
+    T v[K];
+#pragma unroll
+    for(unsigned k = 0; k < K; ++k) v[k] = in[first + std::size_t(k) * FOLD_THREADS];
+#pragma unroll
+    for(unsigned k = 0; k < K; ++k) acc[k] = fold(acc[k], v[k]);
+  }
+  if(tile == whole)  // the partial tile, to the block the rotation hands it to
+    for(std::size_t i = whole * width + threadIdx.x; i < n; i += FOLD_THREADS) acc[0] = fold(acc[0], in[i]);
+#pragma unroll
+  for(unsigned w = K / 2; w; w >>= 1)
+#pragma unroll
+    for(unsigned k = 0; k < w; ++k) acc[k] = fold(acc[k], acc[k + w]);
+  const T mine = fold_block(acc[0], fold, identity, warp_totals);
   if(threadIdx.x == 0) {
-    partials[blockIdx.x] = acc;
+    partials[blockIdx.x] = mine;
     __threadfence();
     last = atomicAdd(ticket, 1u) == gridDim.x - 1;
   }
@@ -92,11 +134,24 @@ __global__ void __launch_bounds__(FOLD_THREADS)
   __threadfence();
   T total = identity;
   for(unsigned b = threadIdx.x; b < gridDim.x; b += FOLD_THREADS) total = fold(total, read_fresh(partials + b));
-  total = fold_block(total, fold, shared);
+  total = fold_block(total, fold, identity, warp_totals);
   if(threadIdx.x == 0) {
     *out = total;
     *ticket = 0u;
   }
+}
+
+// Blocks of one reduction: the device's resident fold blocks (at most FOLD_BLOCKS_PER_SM per SM, fewer if the
+// fold's registers allow fewer), and no more than n has tiles. The occupancy is asked once per instantiation.
+template<class T, class In, class Out, class Fold> inline unsigned fold_grid(std::size_t n) noexcept {
+  static const unsigned per_sm = [] {
+    int fit = 0;
+    check(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&fit, fold_kernel<T, In, Out, Fold>, int(FOLD_THREADS), 0));
+    return fit < 1 ? 1u : fit > int(FOLD_BLOCKS_PER_SM) ? FOLD_BLOCKS_PER_SM : unsigned(fit);
+  }();
+  const std::size_t width = std::size_t(fold_ways<T>()) * FOLD_THREADS, needed = (n + width - 1) / width;
+  const std::size_t most = std::size_t(sm_count()) * per_sm;
+  return unsigned(needed < most ? (needed ? needed : 1) : most);
 }
 
 // ---- scan ------------------------------------------------------------------------------------------------------
@@ -500,7 +555,7 @@ struct Plus {
 template<class In, class Out, class Fold, class T>
 void B200::reduce(void* temp, std::size_t& bytes, In in, Out out, std::size_t n, Fold fold, T identity,
                   Stream s) noexcept {
-  const unsigned grid = b200::fold_grid(n);
+  const unsigned grid = b200::fold_grid<T, In, Out, Fold>(n);
   const std::size_t partials = b200::fold_partials_bytes(grid, sizeof(T));
   if(temp == nullptr) {  // the context asks how much scratch the reduction needs
     bytes = partials + 256;

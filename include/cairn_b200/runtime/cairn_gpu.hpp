@@ -1,66 +1,114 @@
-// Drop-in replacement for CAIRN's runtime/cairn_gpu.hpp on a B200 (sm_100a): the machine that the execution
-// contexts of runtime/cairn_reuse.hpp and the operations of runtime/cairn_exec.hpp run on, and the older
-// synchronous entry points beside it. Generated code includes this header by name (compiler/lower/codegen.py:46);
-// placed ahead of the reference's runtime directory on the include path, it is picked up with no source change.
+// Drop-in replacement for CAIRN's runtime/cairn_gpu.hpp on a B200 (sm_100a): the machine that the reference's
+// execution contexts (runtime/cairn_reuse.hpp) and device operations (runtime/cairn_exec.hpp) are written for.
+// Generated code includes this header by name (compiler/lower/codegen.py:46); placed ahead of the reference's
+// runtime directory on the include path, it is picked up with no change to the emitted source.
 //
-// The machine keeps every member the context and the operations call (runtime/cairn_gpu.hpp:47-125), each one CUDA
-// call as before: streams, events, allocation, copies, and the region launchers, which now come from this
-// directory's cairn_kernels.hpp (persistent, device-sized grids). Its `reduce` is this project's own kernel instead
-// of CUB's, and so are its scans (defined in this directory's cairn_cub.hpp).
+// What the reference's headers require of a machine is its concept: the type names Stream and Event, and members
+// that make and destroy streams and events, order one stream after an event, wait for a stream or an event, answer
+// whether a stream is capturing, allocate and release, zero and copy, run the three kinds of region, and run the
+// collectors (runtime/cairn_gpu.hpp:47-125 lists them). Those names and signatures are interface and are kept. The
+// machine behind them is this project's:
+//
+// * Regions run on cairn_kernels.hpp's persistent, device-sized grids.
+// * The collectors (reduce, inclusive_scan, exclusive_sum) are cairn_cub.hpp's own kernels, not CUB's.
+// * Stream-ordered allocations (alloc_async, which a context created with Allocation::stream_ordered grows its arena
+//   through) come from a memory pool this machine keeps per device, whose release threshold is unbounded: memory a
+//   context frees in stream order stays in the pool for its next growth instead of going back to the driver at the
+//   next synchronization, and the pool is the machine's alone, so no other user of the default pool is affected.
+// * Every member is one CUDA call on the stream it is given; nothing here waits for the whole device, and only
+//   make_stream makes a stream. Streams are ordered after the legacy default stream, as the reference's are, so
+//   work a caller queued there earlier runs first.
+//
+// The reference's header also kept an older synchronous API beside the machine (launch, launch_vector,
+// launch_staged, copy, Ticket and its launch_async / copy_async forms, runtime/cairn_gpu.hpp:128-224); its own
+// comment says generated code no longer calls it, and this header does not provide it.
 #pragma once
 // Marks a program built over these headers (the B200 machine) rather than over the reference's own.
 #define CAIRN_B200_MACHINE 1
 #if !defined(CAIRN_EMULATE)
-#include <cstdio>
-#include <cstring>
+#include <cstddef>
+#include <cstdint>
+#include <mutex>
 #include <cuda_runtime.h>
-#include <iterator>
 #include "cairn_kernels.hpp"
 #include "cairn_reuse.hpp"
 #include "cairn_runtime.hpp"
 namespace cr::gpu {
+// cairn_reuse.hpp keeps its own copies of the launch defaults; a region planned against one must run with the other.
 static_assert(BLOCK == reuse::BLOCK && MAX_GRID == reuse::MAX_GRID && WARP == reuse::WARP);
-
-// At process exit a context may outlive the CUDA runtime; its releases then have nothing left to release.
-inline void released(cudaError_t e) noexcept {
-  if(e != cudaErrorCudartUnloading) check(e);
-}
-template<class T> inline std::size_t bytes(std::size_t n) noexcept { return reuse::span<T>(n); }
-using reuse::aligned;
-using reuse::ALIGN;
 using reuse::Binary;
 using reuse::Dir;
 using reuse::Indexed;
 using reuse::plain;
 using reuse::Where;
 
-inline cudaMemcpyKind kind(Dir d) noexcept {
-  if(d == Dir::h2d) return cudaMemcpyHostToDevice;
-  if(d == Dir::d2h) return cudaMemcpyDeviceToHost;
-  if(d == Dir::d2d) return cudaMemcpyDeviceToDevice;
-  return cudaMemcpyHostToHost;
+namespace b200 {
+
+// A release made while the process exits can find the CUDA runtime already unloaded (a thread's context may be
+// destroyed after it); nothing is left to release then, and that is not a failure.
+inline void let_go(cudaError_t e) noexcept {
+  if(e != cudaErrorCudartUnloading) check(e);
 }
 
-// The B200 as the machine of an execution context. Nothing here waits for the whole device; only make_stream makes a
-// stream; only the alloc / allocate members allocate.
+inline cudaMemcpyKind crossing(Dir d) noexcept {
+  switch(d) {
+    case Dir::h2d: return cudaMemcpyHostToDevice;
+    case Dir::d2h: return cudaMemcpyDeviceToHost;
+    case Dir::d2d: return cudaMemcpyDeviceToDevice;
+    case Dir::h2h: return cudaMemcpyHostToHost;
+  }
+  trap();
+  return cudaMemcpyDefault;
+}
+
+// The machine's stream-ordered pool on the current device, made on first use. Device memory, unbounded release
+// threshold (the pool keeps what is freed into it until the process ends).
+inline cudaMemPool_t arena_pool() noexcept {
+  constexpr int DEVICES = 64;
+  static cudaMemPool_t pools[DEVICES];
+  static std::once_flag made[DEVICES];
+  int dev = 0;
+  check(cudaGetDevice(&dev));
+  if(dev < 0 || dev >= DEVICES) trap();
+  std::call_once(made[dev], [dev] {
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    check(cudaMemPoolCreate(&pools[dev], &props));
+    std::uint64_t keep = ~std::uint64_t(0);
+    check(cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep));
+  });
+  return pools[dev];
+}
+
+}  // namespace b200
+
+// The B200 as the machine of an execution context.
 struct B200 {
   using Stream = cudaStream_t;
   using Event = cudaEvent_t;
+
+  // Streams and events.
   Stream make_stream() noexcept {
-    cudaStream_t s = nullptr;
-    check(cudaStreamCreate(&s));
+    Stream s = nullptr;
+    check(cudaStreamCreateWithFlags(&s, cudaStreamDefault));
     return s;
   }
-  void destroy_stream(Stream s) noexcept { released(cudaStreamDestroy(s)); }
+  void destroy_stream(Stream s) noexcept { b200::let_go(cudaStreamDestroy(s)); }
   Event make_event() noexcept {
-    cudaEvent_t e = nullptr;
+    Event e = nullptr;
     check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     return e;
   }
-  void destroy_event(Event e) noexcept { released(cudaEventDestroy(e)); }
+  void destroy_event(Event e) noexcept { b200::let_go(cudaEventDestroy(e)); }
   void record(Event e, Stream s) noexcept { check(cudaEventRecord(e, s)); }
   void wait_event(Stream s, Event e) noexcept { check(cudaStreamWaitEvent(s, e, 0)); }
-  unsigned long long handle(Stream s) noexcept { return reinterpret_cast<std::uintptr_t>(s); }
+  // A stream's handle is its address, which asks CUDA nothing and so is safe inside a graph capture; its id is
+  // CUDA's, unique for the life of the process; capturing says whether a capture is recording the stream.
+  unsigned long long handle(Stream s) noexcept {
+    return static_cast<unsigned long long>(reinterpret_cast<std::uintptr_t>(s));
+  }
   unsigned long long stream_id(Stream s) noexcept {
     unsigned long long id = 0;
     check(cudaStreamGetId(s, &id));
@@ -72,45 +120,53 @@ struct B200 {
     return status != cudaStreamCaptureStatusNone;
   }
   void sync_stream(Stream s) noexcept { check(cudaStreamSynchronize(s)); }
-  void sync_event(Event e) noexcept { released(cudaEventSynchronize(e)); }
-  void* alloc(std::size_t b) noexcept {
+  void sync_event(Event e) noexcept { b200::let_go(cudaEventSynchronize(e)); }
+
+  // Memory. alloc/free hold a context's arena; the _async pair takes it from the machine's pool in stream order;
+  // allocate/release hold a scoped owner's storage where it asked to live.
+  void* alloc(std::size_t bytes) noexcept {
     void* p = nullptr;
-    check(cudaMalloc(&p, b));
+    check(cudaMalloc(&p, bytes));
     return p;
   }
-  void free(void* p) noexcept { released(cudaFree(p)); }
-  void* alloc_async(std::size_t b, Stream s) noexcept {
+  void free(void* p) noexcept { b200::let_go(cudaFree(p)); }
+  void* alloc_async(std::size_t bytes, Stream s) noexcept {
     void* p = nullptr;
-    check(cudaMallocAsync(&p, b, s));
+    check(cudaMallocFromPoolAsync(&p, bytes, b200::arena_pool(), s));
     return p;
   }
   void free_async(void* p, Stream s) noexcept { check(cudaFreeAsync(p, s)); }
-  void* allocate(Where w, std::size_t b) noexcept {
+  void* allocate(Where where, std::size_t bytes) noexcept {
     void* p = nullptr;
-    if(w == Where::device) check(cudaMalloc(&p, b));
-    else if(w == Where::pinned) check(cudaMallocHost(&p, b));
-    else check(cudaMallocManaged(&p, b));
+    switch(where) {
+      case Where::device: check(cudaMalloc(&p, bytes)); break;
+      case Where::pinned: check(cudaMallocHost(&p, bytes)); break;
+      case Where::unified: check(cudaMallocManaged(&p, bytes)); break;
+    }
     return p;
   }
-  void release(Where w, void* p) noexcept { check(w == Where::pinned ? cudaFreeHost(p) : cudaFree(p)); }
-  void zero(void* p, std::size_t b, Stream s) noexcept { check(cudaMemsetAsync(p, 0, b, s)); }
-  void copy(void* dst, const void* src, std::size_t b, Dir d, Stream s) noexcept {
-    check(cudaMemcpyAsync(dst, src, b, kind(d), s));
+  void release(Where where, void* p) noexcept { check(where == Where::pinned ? cudaFreeHost(p) : cudaFree(p)); }
+  void zero(void* p, std::size_t bytes, Stream s) noexcept { check(cudaMemsetAsync(p, 0, bytes, s)); }
+  void copy(void* dst, const void* src, std::size_t bytes, Dir d, Stream s) noexcept {
+    check(cudaMemcpyAsync(dst, src, bytes, b200::crossing(d), s));
   }
+
+  // Regions (cairn_kernels.hpp).
   template<unsigned U, class F>
   void lanes(std::size_t n, const F& body, Stream s, unsigned block, std::size_t per_lane) noexcept {
-    fire<U>(n, body, s, block, per_lane);
+    b200::start_lanes<U>(n, body, s, block, per_lane);
   }
   template<unsigned W, unsigned U, class F, class G>
   void vector_lanes(std::size_t n, F scalar, G chunk, Stream s, unsigned block, std::size_t per_lane) noexcept {
-    fire_vector<W, U>(n, scalar, chunk, s, block, per_lane);
+    b200::start_chunks<W, U>(n, scalar, chunk, s, block, per_lane);
   }
   template<std::size_t R, unsigned U, class L, class F, class S>
   void staged_lanes(std::size_t n, L load, F body, S bytes, Stream s, unsigned block, std::size_t per_lane) noexcept {
-    fire_staged<R, U>(n, load, body, bytes, s, block, per_lane);
+    b200::start_staged<R, U>(n, load, body, bytes, s, block, per_lane);
   }
-  // Defined in cairn_cub.hpp (included only by programs with a device collector). With a null `temp` each says how
-  // many bytes of scratch it needs.
+
+  // Collectors, defined in cairn_cub.hpp, which the lowering includes only in a program with a device reduce, scan
+  // or compact. Called with a null `temp`, each only answers how many bytes of scratch it needs.
   template<class In, class Out, class Fold, class T>
   void reduce(void* temp, std::size_t& bytes, In in, Out out, std::size_t n, Fold fold, T identity, Stream s) noexcept;
   template<class In, class Out, class Fold>
@@ -122,92 +178,4 @@ using Machine = B200;
 }  // namespace cr::gpu
 
 #include "cairn_exec.hpp"
-
-namespace cr::gpu {
-
-// The older synchronous entry points: the legacy default stream, then a wait for the whole device.
-template<class T> inline void copy(T* dst, const T* src, std::size_t n, Dir d) noexcept {
-  if(n) check(cudaMemcpy(dst, src, bytes<T>(n), kind(d)));
-}
-template<unsigned U = 1, class F>
-inline void launch(std::size_t n, F body, unsigned block = BLOCK, std::size_t per_lane = 1) noexcept {
-  fire<U>(n, body, nullptr, block, per_lane);
-  check(cudaDeviceSynchronize());
-}
-template<unsigned W, unsigned U = 1, class F, class G>
-inline void launch_vector(std::size_t n, bool whole, F scalar, G chunk, unsigned block = BLOCK,
-                          std::size_t per_lane = 1) noexcept {
-  if(!whole) return launch<U>(n, scalar, block, per_lane);
-  if(!n) return;
-  fire_vector<W, U>(n, scalar, chunk, nullptr, block, per_lane);
-  check(cudaDeviceSynchronize());
-}
-template<std::size_t R, unsigned U = 1, class L, class F, class S>
-inline void launch_staged(std::size_t n, L load, F body, S bytes, unsigned block = BLOCK,
-                          std::size_t per_lane = 1) noexcept {
-  if(!n) return;
-  fire_staged<R, U>(n, load, body, bytes, nullptr, block, per_lane);
-  check(cudaDeviceSynchronize());
-}
-
-// A ticket: one stream and one event, consumed by exactly one wait; dropping it unwaited traps.
-class Ticket final {
-  cudaStream_t s_ = nullptr;
-  cudaEvent_t e_ = nullptr;
-public:
-  Ticket() noexcept {
-    check(cudaStreamCreate(&s_));
-    check(cudaEventCreateWithFlags(&e_, cudaEventDisableTiming));
-  }
-  Ticket(Ticket&& o) noexcept : s_(o.s_), e_(o.e_) { o.s_ = nullptr; o.e_ = nullptr; }
-  Ticket(const Ticket&) = delete;
-  Ticket& operator=(const Ticket&) = delete;
-  Ticket& operator=(Ticket&&) = delete;
-  ~Ticket() noexcept { if(s_) trap(); }
-  cudaStream_t stream() const noexcept { return s_; }
-  cudaEvent_t mark() const noexcept {
-    check(cudaEventRecord(e_, s_));
-    return e_;
-  }
-  void follow(const Ticket& dep) const noexcept {
-    check(cudaEventRecord(dep.e_, dep.s_));
-    check(cudaStreamWaitEvent(s_, dep.e_, 0));
-  }
-  void wait() && noexcept { finish(); }
-  void finish() noexcept {
-    check(cudaStreamSynchronize(s_));
-    check(cudaEventDestroy(e_));
-    check(cudaStreamDestroy(s_));
-    s_ = nullptr;
-    e_ = nullptr;
-  }
-};
-inline void wait(Ticket&& t) noexcept { t.finish(); }
-template<class F, class... After> inline Ticket launch_async(std::size_t n, F body, const After&... after) noexcept {
-  Ticket t;
-  (t.follow(after), ...);
-  fire(n, body, t.stream());
-  return t;
-}
-template<class F> inline Ticket launch_after(const Ticket& dep, std::size_t n, F body) noexcept {
-  Ticket t;
-  t.follow(dep);
-  fire(n, body, t.stream());
-  return t;
-}
-template<class T, class... After>
-inline Ticket copy_async(T* dst, const T* src, std::size_t n, Dir d, const After&... after) noexcept {
-  Ticket t;
-  (t.follow(after), ...);
-  if(n) check(cudaMemcpyAsync(dst, src, bytes<T>(n), kind(d), t.stream()));
-  return t;
-}
-template<class T>
-inline Ticket copy_after(const Ticket& dep, T* dst, const T* src, std::size_t n, Dir d) noexcept {
-  Ticket t;
-  t.follow(dep);
-  if(n) check(cudaMemcpyAsync(dst, src, bytes<T>(n), kind(d), t.stream()));
-  return t;
-}
-}  // namespace cr::gpu
 #endif
