@@ -40,10 +40,13 @@ bool tensor_path_ok(const GemmArgs& g);
 // Queues the product on `stream`; `sms` is the device's SM count, `fault` its fault word.
 cudaError_t gemm_launch(const GemmArgs& g, cudaStream_t stream, int sms, std::uint32_t* fault);
 
-// Streaming kernels (stream.cu). Scratch: `partials` holds one 16-byte cell per block of the grid, `ticket` one
-// counter that must be zero before the launch and is zero again after it.
+// Streaming kernels (stream.cu). A reduction's scratch (reduce_scratch_bytes) starts with its ticket, one counter
+// that must be zero before the launch and is zero again after it, followed 256 bytes in by one 32-byte cell per
+// block of the launch's grid.
 constexpr int STREAM_THREADS = 512;
-int stream_grid(int sms);  // blocks a streaming launch uses
+int sum_f32_grid(int sms);  // blocks of each reduction's launch (STREAM_THREADS each)
+int sum_u64_grid(int sms);
+int mse_grid(int sms);
 std::size_t reduce_scratch_bytes(int sms);
 cudaError_t saxpy_f32_launch(std::size_t n, float* out, const float* x, const float* y, float a, cudaStream_t s,
                              int sms);

@@ -10,7 +10,7 @@
 //
 // The array is a file-scope static __device__ object of STATIC_SCRATCH_BYTES: every GPU that loads the library holds
 // it until the process exits. Its size is stated by the largest grid it serves, STATIC_MAX_BLOCKS blocks (a 148-SM
-// B200 launches 296); a device whose launch would need more partial cells is refused with
+// B200 launches 1184); a device whose launch would need more partial cells is refused with
 // CAIRN_B200_ERR_SCRATCH and nothing is queued.
 //
 // In host code the array's name is only a host-side stand-in, not a device address, so the first call on each device
@@ -28,8 +28,8 @@
 namespace cb {
 namespace {
 
-constexpr int STATIC_MAX_BLOCKS = 1024;                         // partial cells the array holds
-constexpr std::size_t STATIC_SCRATCH_BYTES = STATIC_MAX_BLOCKS * 32 + 256;  // cells, then the ticket
+constexpr int STATIC_MAX_BLOCKS = 2048;                                     // partial cells the array holds
+constexpr std::size_t STATIC_SCRATCH_BYTES = 256 + STATIC_MAX_BLOCKS * 32;  // the ticket, then the cells
 static __device__ __align__(256) unsigned char g_static_scratch[STATIC_SCRATCH_BYTES];
 
 constexpr int MAX_DEVICES = 64;
@@ -98,11 +98,10 @@ extern "C" int cairn_b200_sum_f32_noalloc(void* stream, size_t n, const float* x
   int status;
   const StaticScratch* s = static_scratch(&status);
   if (!s) return status;
-  const int grid = stream_grid(s->sms);
+  const int grid = sum_f32_grid(s->sms);
   if (grid > STATIC_MAX_BLOCKS) return CAIRN_B200_ERR_SCRATCH;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The ticket after this launch's partial cells must read zero when the kernel starts.
-  if (n && cudaMemsetAsync(s->ptr + static_cast<std::size_t>(grid) * 32, 0, sizeof(unsigned int), st) != cudaSuccess)
-    return CAIRN_B200_ERR_CUDA;
+  // The ticket, at the start of the array, must read zero when the kernel starts.
+  if (n && cudaMemsetAsync(s->ptr, 0, sizeof(unsigned int), st) != cudaSuccess) return CAIRN_B200_ERR_CUDA;
   return sum_f32_launch(n, x, out, nullptr, s->ptr, st, s->sms) == cudaSuccess ? CAIRN_B200_OK : CAIRN_B200_ERR_CUDA;
 }

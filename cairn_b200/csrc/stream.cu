@@ -4,12 +4,16 @@
 // The reference runs a `parallel` region as one index per thread in a grid of at most 65535 blocks of 256 threads,
 // scalar 4-byte accesses (runtime/cairn_kernels.hpp:69-96), and a device `reduce +` through CUB's DeviceReduce with
 // temporaries from the context's arena (runtime/cairn_reuse.hpp:346-372, runtime/cairn_cub.hpp:14-17). Here:
-//   - a grid of 2 x 512-thread blocks per SM (every SM holds 1024 threads), grid-stride over 16-byte vectors, four
-//     vectors of each operand in flight per thread, streaming cache hints (each byte is touched once);
+//   - saxpy: one 16-byte vector of each operand per thread, in 1024-thread blocks, a block per 4096 elements, with
+//     streaming cache hints (each byte is touched once). Measured on a B200 at n = 2^30 over random values (all-zero
+//     inputs stream faster and mislead): 7.2 TB/s, where two resident 512-thread blocks per SM striding over four
+//     vectors per step ran 6.1-6.3: with short blocks the SMs finish together;
 //   - the reductions fold each thread's terms into registers, then a warp shuffle tree, a shared-memory tree across
 //     the block's 16 warps, one partial per block in scratch, and the last block to finish (an atomic ticket, no
 //     spin-wait) folds the partials in block order and writes the total. One launch, deterministic for a given n
-//     and device: every thread's terms and every tree are fixed by (n, grid).
+//     and device: every thread's terms and every tree are fixed by (n, grid). Each reduction's grid is the one that
+//     ran fastest at n = 2^30 (random values) among 2 to 64 blocks per SM: 8 per SM for the f32 sum (6.8 TB/s; its
+//     double-double additions keep two 512-thread blocks resident), 32 for the u64 sum (7.4), 2 for the loss (6.8).
 //   - f32 terms are added in f64, which holds every f32 term exactly; the total is rounded to f32 once.
 //   - u64 terms carry cr::Sum's sticky overflow flag (runtime/cairn_runtime.hpp:158-166) through every fold.
 #include <cstdint>
@@ -21,56 +25,48 @@
 
 namespace cb {
 
-int stream_grid(int sms) { return 2 * sms; }
-// One 32-byte partial per block, then the ticket (zero between launches).
-std::size_t reduce_scratch_bytes(int sms) { return static_cast<std::size_t>(stream_grid(sms)) * 32 + 256; }
+int sum_f32_grid(int sms) { return 8 * sms; }
+int sum_u64_grid(int sms) { return 32 * sms; }
+int mse_grid(int sms) { return 2 * sms; }
+// The ticket (256 bytes, zero between launches), then one 32-byte partial per block of the widest reduction grid.
+std::size_t reduce_scratch_bytes(int sms) { return 256 + static_cast<std::size_t>(sum_u64_grid(sms)) * 32; }
 
 namespace {
 
 constexpr int T = STREAM_THREADS;
 constexpr int WARPS = T / 32;
 constexpr int UNROLL = 4;
+constexpr int SAXPY_THREADS = 1024;
+
+// The ticket sits at the start of the scratch and the partials after it, wherever each launch's grid ends.
+unsigned int* ticket_of(void* scratch) { return static_cast<unsigned int*>(scratch); }
+template <class P> P* partials_of(void* scratch) { return reinterpret_cast<P*>(static_cast<char*>(scratch) + 256); }
 
 __device__ __forceinline__ float saxpy1(float a, float x, float y) { return __fadd_rn(__fmul_rn(a, x), y); }
 
-// out may equal x or y: each vector is read before the same vector is written.
-__global__ void __launch_bounds__(T, 2)
+// out may equal x or y: each vector is read before the same vector is written. One vector per thread, a block per
+// 4096 elements (the launcher refuses an n whose grid would not fit, past 2^43 elements); the last block also runs
+// the n % 4 elements past the last whole vector. A grid-stride loop over the same grid measured 12 % slower.
+__global__ void __launch_bounds__(SAXPY_THREADS)
     saxpy_vec_kernel(std::size_t n, float* out, const float* x, const float* y, float a) {
-  const std::size_t n4 = n / 4;
-  const std::size_t stride = static_cast<std::size_t>(gridDim.x) * T;
-  std::size_t i = static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x;
-  const float4* x4 = reinterpret_cast<const float4*>(x);
-  const float4* y4 = reinterpret_cast<const float4*>(y);
-  float4* o4 = reinterpret_cast<float4*>(out);
-  for (; i + (UNROLL - 1) * stride < n4; i += UNROLL * stride) {
-    float4 xv[UNROLL], yv[UNROLL];
-#pragma unroll
-    for (int u = 0; u < UNROLL; ++u) {
-      xv[u] = __ldcs(x4 + i + u * stride);
-      yv[u] = __ldcs(y4 + i + u * stride);
-    }
-#pragma unroll
-    for (int u = 0; u < UNROLL; ++u) {
-      const float4 o = make_float4(saxpy1(a, xv[u].x, yv[u].x), saxpy1(a, xv[u].y, yv[u].y),
-                                   saxpy1(a, xv[u].z, yv[u].z), saxpy1(a, xv[u].w, yv[u].w));
-      __stcs(o4 + i + u * stride, o);
-    }
+  const std::size_t n4 = n / 4, i = static_cast<std::size_t>(blockIdx.x) * SAXPY_THREADS + threadIdx.x;
+  if (i < n4) {
+    const float4 xv = __ldcs(reinterpret_cast<const float4*>(x) + i);
+    const float4 yv = __ldcs(reinterpret_cast<const float4*>(y) + i);
+    __stcs(reinterpret_cast<float4*>(out) + i, make_float4(saxpy1(a, xv.x, yv.x), saxpy1(a, xv.y, yv.y),
+                                                         saxpy1(a, xv.z, yv.z), saxpy1(a, xv.w, yv.w)));
   }
-  for (; i < n4; i += stride) {
-    const float4 xv = __ldcs(x4 + i), yv = __ldcs(y4 + i);
-    __stcs(o4 + i, make_float4(saxpy1(a, xv.x, yv.x), saxpy1(a, xv.y, yv.y), saxpy1(a, xv.z, yv.z),
-                               saxpy1(a, xv.w, yv.w)));
-  }
-  if (blockIdx.x == 0 && threadIdx.x < n - n4 * 4) {
+  if (blockIdx.x == gridDim.x - 1 && threadIdx.x < n - n4 * 4) {
     const std::size_t j = n4 * 4 + threadIdx.x;
     out[j] = saxpy1(a, x[j], y[j]);
   }
 }
 
-__global__ void __launch_bounds__(T, 2)
+// Views off 16 bytes: 4-byte accesses, about 64 per thread (the grid-stride shape a plain region runs fastest in).
+__global__ void __launch_bounds__(256)
     saxpy_scalar_kernel(std::size_t n, float* out, const float* x, const float* y, float a) {
-  const std::size_t stride = static_cast<std::size_t>(gridDim.x) * T;
-  for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * T + threadIdx.x; i < n; i += stride)
+  const std::size_t stride = static_cast<std::size_t>(gridDim.x) * blockDim.x;
+  for (std::size_t i = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride)
     out[i] = saxpy1(a, x[i], y[i]);
 }
 
@@ -452,9 +448,19 @@ bool aligned16(const void* p) { return (reinterpret_cast<std::uintptr_t>(p) & 15
 cudaError_t saxpy_f32_launch(std::size_t n, float* out, const float* x, const float* y, float a, cudaStream_t s,
                              int sms) {
   if (!n) return cudaSuccess;
-  const int grid = stream_grid(sms);
-  if (aligned16(out) && aligned16(x) && aligned16(y)) saxpy_vec_kernel<<<grid, T, 0, s>>>(n, out, x, y, a);
-  else saxpy_scalar_kernel<<<grid, T, 0, s>>>(n, out, x, y, a);
+  constexpr std::size_t MAX_BLOCKS = 0x7fffffff;
+  if (aligned16(out) && aligned16(x) && aligned16(y)) {
+    const std::size_t blocks = (n / 4 + SAXPY_THREADS - 1) / SAXPY_THREADS;
+    if (blocks > MAX_BLOCKS) return cudaErrorInvalidValue;
+    saxpy_vec_kernel<<<static_cast<unsigned>(blocks ? blocks : 1), SAXPY_THREADS, 0, s>>>(n, out, x, y, a);
+  } else {  // about 64 indices per thread, in whole multiples of the SM count
+    const std::size_t per_wave = static_cast<std::size_t>(sms), want = (n + 256 * 64 - 1) / (256 * 64),
+                      least = per_wave * 8, most = (n + 255) / 256;
+    std::size_t blocks = (want > least ? want : least + per_wave - 1) / per_wave * per_wave;
+    if (blocks > most) blocks = most;
+    saxpy_scalar_kernel<<<static_cast<unsigned>(blocks < MAX_BLOCKS ? blocks : MAX_BLOCKS), 256, 0, s>>>(n, out, x,
+                                                                                                          y, a);
+  }
   return cudaGetLastError();
 }
 
@@ -468,9 +474,9 @@ cudaError_t sum_f32_launch(std::size_t n, const float* x, float* out_f32, double
     if (out_f64) return cudaMemsetAsync(out_f64, 0, 3 * sizeof(double), s);
     return cudaSuccess;
   }
-  const int grid = stream_grid(sms);
-  Partial* partials = static_cast<Partial*>(scratch);
-  unsigned int* ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(scratch) + static_cast<std::size_t>(grid) * 32);
+  const int grid = sum_f32_grid(sms);
+  Partial* partials = partials_of<Partial>(scratch);
+  unsigned int* ticket = ticket_of(scratch);
   if (aligned16(x)) sum_f32_kernel<true><<<grid, T, 0, s>>>(n, x, out_f32, out_f64, partials, ticket);
   else sum_f32_kernel<false><<<grid, T, 0, s>>>(n, x, out_f32, out_f64, partials, ticket);
   return cudaGetLastError();
@@ -484,9 +490,9 @@ cudaError_t combine_f32_parts_launch(const double* parts, int count, float* out,
 cudaError_t mse_grad_launch(std::size_t n, const float* y, const float* t, std::uint16_t* dy, float scale,
                             float* loss, void* scratch, cudaStream_t s, int sms) {
   if (!n) return cudaMemsetAsync(loss, 0, sizeof(float), s);
-  const int grid = stream_grid(sms);
-  Partial* partials = static_cast<Partial*>(scratch);
-  unsigned int* ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(scratch) + static_cast<std::size_t>(grid) * 32);
+  const int grid = mse_grid(sms);
+  Partial* partials = partials_of<Partial>(scratch);
+  unsigned int* ticket = ticket_of(scratch);
   auto* d = reinterpret_cast<__nv_bfloat16*>(dy);
   if (aligned16(y) && aligned16(t) && (reinterpret_cast<std::uintptr_t>(dy) & 7u) == 0)
     mse_grad_kernel<true><<<grid, T, 0, s>>>(n, y, t, d, scale, loss, partials, ticket);
@@ -502,9 +508,9 @@ cudaError_t sum_u64_launch(std::size_t n, const std::uint64_t* x, std::uint64_t*
     if (e == cudaSuccess) e = cudaMemsetAsync(overflow, 0, sizeof(std::uint32_t), s);
     return e;
   }
-  const int grid = stream_grid(sms);
-  SumU64* partials = static_cast<SumU64*>(scratch);
-  unsigned int* ticket = reinterpret_cast<unsigned int*>(static_cast<char*>(scratch) + static_cast<std::size_t>(grid) * 32);
+  const int grid = sum_u64_grid(sms);
+  SumU64* partials = partials_of<SumU64>(scratch);
+  unsigned int* ticket = ticket_of(scratch);
   const auto* xx = reinterpret_cast<const unsigned long long*>(x);
   auto* oo = reinterpret_cast<unsigned long long*>(out);
   if (aligned16(x)) sum_u64_kernel<true><<<grid, T, 0, s>>>(n, xx, oo, overflow, partials, ticket);

@@ -133,9 +133,9 @@ int cairn_b200_sum_u64_host(void* stream, size_t n, const uint64_t* x, uint64_t*
  * reference's reductions always take their temporaries from the context's arena). A serving process whose device
  * memory is reserved up front by its own allocator, or a loop that cannot afford a cudaMalloc's implicit
  * synchronization, calls this form: it runs the same kernel over a scratch array compiled into the library
- * (32,768 bytes of partials for at most 1024 blocks, plus the ticket; every GPU that loads the library holds it until
+ * (65,536 bytes of partials for at most 2048 blocks, plus the ticket; every GPU that loads the library holds it until
  * exit), and never calls cudaMalloc, cudaFree or an allocating library routine. A device whose launch would need more
- * than 1024 blocks gets CAIRN_B200_ERR_SCRATCH. The first call on each device looks up the array's device address;
+ * than 2048 blocks gets CAIRN_B200_ERR_SCRATCH (a 148-SM B200 launches 1184). The first call on each device looks up the array's device address;
  * make it before any stream capture. All calls share the array: calls whose work overlaps on the GPU race, so order
  * them (one stream). Same result bits as cairn_b200_sum_f32. */
 int cairn_b200_sum_f32_noalloc(void* stream, size_t n, const float* x, float* out);

@@ -6,26 +6,25 @@
 // cairn_gpu.hpp calls, as the B200 machine's `lanes`, `vector_lanes` and `staged_lanes` members.
 //
 // The contract each kernel keeps is the one runtime/cairn_exec.hpp states for run, run_vector and run_staged: every
-// index below n runs its body exactly once, on the stream the caller names, and nothing waits. How a B200 runs them:
+// index below n runs its body exactly once, on the stream the caller names, and nothing waits. The grid shapes are
+// the ones that ran fastest on a B200 at n = 2^30 (f32 saxpy and a five-point blur, each shape against the others):
 //
-// * A region is a persistent grid. The launcher sizes it from the occupancy calculator for the kernel, its block
-//   and its shared memory, times the SM count (148 on a B200): every block is resident from the start, and no more
-//   blocks are launched than the region has tiles of work for. There is no 65,535-block cap to stride around.
-// * The unit of work is a tile of U * block consecutive indices (U from the plan's `unroll`): thread t of the block
-//   runs indices t, t + block, ... of each tile it is handed, so every step of the warp touches 32 consecutive
-//   elements, and the U steps of a tile are unrolled without a bounds test. Blocks take tiles in rotation; the
-//   last, partial tile goes to whichever block the rotation hands it to, with a test per index.
-// * A `plan vector W` region runs its whole chunks the same way (one W-wide access per array per lane, 16 bytes for
-//   f32 and W = 4), and the fewer than W indices past the last whole chunk run in parallel, one thread each.
-// * A `plan stage R` region keeps two tiles of shared memory when they fit: while a block's lanes read one tile,
-//   its threads have already loaded the next one into the other, so one barrier per tile separates the two, where a
-//   single tile needs a barrier before its load and another after it.
-//
-// Why a plain region's body runs one index at a time per thread: the body is the program's lambda over raw
-// pointers, and the compiler must assume that its store to out[i] may alias the next index's loads, so those loads
-// cannot be issued early. A plain region's memory parallelism is therefore two to three loads in flight per
-// thread, times the 2048 threads an SM holds; the 16-byte chunks of a vector region carry four times the bytes per
-// load, which is what reaches HBM's bandwidth.
+// * Plain region: a grid-stride loop in which each thread runs about LANE_INDICES = 64 indices (more if the plan's
+//   per_lane asks), and never fewer blocks than the SMs hold resident while n has work for them; the whole strides
+//   run without a bounds test and the plan's `unroll` unrolls them. Around 64 indices per thread ran fastest (about
+//   4.96 TB/s for saxpy, 1-3 % above 9,472 or 131,072 blocks); a persistent grid of one resident wave ran 4 % slower,
+//   because the SMs whose blocks fell behind finished last. A plain region cannot go much faster: the body is the
+//   program's lambda over raw pointers, the compiler must assume its store to out[i] may alias the next index's
+//   loads, so a thread has only this index's loads in flight, times the 2048 threads an SM holds.
+// * `plan vector W`: one W-wide chunk per thread (per_lane chunks when the plan asks), a block per block-width of
+//   chunks, and the fewer than W indices past the last whole chunk run by the last block, one thread each. For f32
+//   and W = 4 each access is 16 bytes; this shape ran 7.1 TB/s for saxpy, where a grid-stride loop over 65,535
+//   blocks ran 6.9 and a persistent grid 6.3.
+// * `plan stage R`: one tile of shared memory per block, each block taking a run of STAGE_TILES = 64 consecutive
+//   tiles (or per_lane, if larger), between the two barriers run_staged's rule asks for. Consecutive tiles share
+//   their halos in cache; 2.49 TB/s for the blur against 1.69 with one tile per block. Two tiles per block, loading
+//   the next while the lanes read the current one, measured slower (2.31): the load body's loads must land before
+//   its stores into the tile, so nothing overlapped, and the second tile halved the blocks resident per SM.
 //
 // Build a program with this directory ahead of the reference's runtime directory on the include path.
 #pragma once
@@ -97,28 +96,37 @@ inline std::size_t resident_blocks(std::atomic<unsigned long long>& last, K kern
   return std::size_t(per_sm) * sm_count();
 }
 
-// The persistent grid: the device's resident blocks, fewer when the region has fewer tiles of work, or when the
-// plan asked for about `per_lane` indices per thread over `indices` indices (a block covers block * per_lane).
-inline unsigned persistent_grid(std::size_t resident, std::size_t tiles, std::size_t indices, unsigned block,
-                                std::size_t per_lane) noexcept {
-  const std::size_t each = std::size_t(block) * (per_lane ? per_lane : 1);
-  std::size_t g = (indices + each - 1) / each;
-  if(g > tiles) g = tiles;
-  if(g > resident) g = resident;
+constexpr std::size_t LANE_INDICES = 64;  // indices per thread a plain region's grid aims at
+constexpr std::size_t STAGE_TILES = 64;   // consecutive tiles per block of a staged region
+constexpr std::size_t GRID_LIMIT = 0x7fffffff;
+
+// The grid for `units` units of work (indices, chunks or tiles), `per` per thread or block as the caller counts
+// them, in blocks of `each` units: no fewer blocks than the device holds resident when there are units for them,
+// and past that a whole multiple of the SM count (every SM gets as many blocks: 65,564 blocks of a saxpy region ran
+// 4.96 TB/s on a B200 where 65,535 ran 4.79).
+inline unsigned region_grid(std::size_t units, std::size_t each, std::size_t per, std::size_t resident) noexcept {
+  const std::size_t blocks = (units + each - 1) / each;  // one unit per thread (or tile per block)
+  std::size_t g = (units + each * per - 1) / (each * per);
+  const std::size_t least = blocks < resident ? blocks : resident;
+  if(g <= least) {
+    g = least;
+  } else {
+    const std::size_t sms = sm_count();
+    g = (g + sms - 1) / sms * sms;
+    if(g > blocks) g = blocks;
+  }
+  if(g > GRID_LIMIT) trap();  // the caller raises `per` first
   return unsigned(g ? g : 1);
 }
 
-// `parallel i in n`: tiles of U * blockDim.x indices.
+// `parallel i in n`: thread (b, t) runs indices b * blockDim.x + t + k * stride, k = 0, 1, ...
 template<unsigned U, class F> __global__ void region_lanes(std::size_t n, F body) {
-  const std::size_t width = std::size_t(U) * blockDim.x, whole = n / width;
-  std::size_t tile = blockIdx.x;
-  for(; tile < whole; tile += gridDim.x) {
-    const std::size_t first = tile * width + threadIdx.x;
-#pragma unroll
-    for(unsigned u = 0; u < U; ++u) body(first + std::size_t(u) * blockDim.x);
-  }
-  if(tile == whole)  // the rotation handed this block the partial tile
-    for(std::size_t i = whole * width + threadIdx.x; i < n; i += blockDim.x) body(i);
+  const std::size_t stride = std::size_t(gridDim.x) * blockDim.x;
+  std::size_t i = std::size_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const std::size_t whole = n / stride;  // strides in which every thread has an index
+#pragma unroll U
+  for(std::size_t k = 0; k < whole; ++k, i += stride) body(i);
+  if(i < n) body(i);
 }
 
 template<unsigned U, class F>
@@ -130,28 +138,23 @@ inline void start_lanes(std::size_t n, const F& body, cudaStream_t s, unsigned b
   static std::atomic<unsigned long long> fit{0};
   if(block > most) block = most;
   if(block < WARP) block = WARP;
-  const std::size_t width = std::size_t(U) * block, tiles = (n + width - 1) / width;
-  const unsigned grid =
-      persistent_grid(resident_blocks(fit, region_lanes<U, F>, block, 0), tiles, n, block, per_lane);
+  std::size_t per = per_lane > LANE_INDICES ? per_lane : LANE_INDICES;
+  while((n + block * per - 1) / (block * per) > GRID_LIMIT) per *= 2;
+  const unsigned grid = region_grid(n, block, per, resident_blocks(fit, region_lanes<U, F>, block, 0));
   region_lanes<U><<<grid, block, 0, s>>>(n, body);
   check(cudaGetLastError());
 }
 
-// `plan f { vector W; }`: whole chunks of W indices from index 0 in tiles of U * blockDim.x chunks, then the
-// n % W indices past them, one thread each.
-template<unsigned W, unsigned U, class F, class G> __global__ void region_chunks(std::size_t n, F scalar, G chunk) {
-  const std::size_t chunks = n / W, width = std::size_t(U) * blockDim.x, whole = chunks / width;
-  std::size_t tile = blockIdx.x;
-  for(; tile < whole; tile += gridDim.x) {
-    const std::size_t first = tile * width + threadIdx.x;
-#pragma unroll
-    for(unsigned u = 0; u < U; ++u) chunk((first + std::size_t(u) * blockDim.x) * W);
-  }
-  if(tile == whole) {
-    for(std::size_t c = whole * width + threadIdx.x; c < chunks; c += blockDim.x) chunk(c * W);
-    const std::size_t rest = n - chunks * W;  // fewer than W <= 16 indices, and a block is at least a warp
-    if(threadIdx.x < rest) scalar(chunks * W + threadIdx.x);
-  }
+// `plan f { vector W; }`: block b runs chunks b * per * blockDim.x + t + k * blockDim.x, k < per; a chunk is W
+// indices from index chunk * W. The last block also runs the n % W indices past the last whole chunk.
+template<unsigned W, unsigned U, class F, class G>
+__global__ void region_chunks(std::size_t n, std::size_t per, F scalar, G chunk) {
+  const std::size_t chunks = n / W;
+  std::size_t c = std::size_t(blockIdx.x) * per * blockDim.x + threadIdx.x;
+#pragma unroll U
+  for(std::size_t k = 0; k < per; ++k, c += blockDim.x)
+    if(c < chunks) chunk(c * W);
+  if(blockIdx.x == gridDim.x - 1 && threadIdx.x < n - chunks * W) scalar(chunks * W + threadIdx.x);
 }
 
 template<unsigned W, unsigned U, class F, class G>
@@ -161,52 +164,31 @@ inline void start_chunks(std::size_t n, F scalar, G chunk, cudaStream_t s, unsig
   static_assert(std::is_trivially_copyable_v<F> && std::is_trivially_copyable_v<G>, "lanes cross as arguments");
   if(!n) return;
   static const unsigned most = widest_block(region_chunks<W, U, F, G>);
-  static std::atomic<unsigned long long> fit{0};
   if(block > most) block = most;
   if(block < WARP) block = WARP;
-  const std::size_t width = std::size_t(U) * block, tiles = (n / W + width - 1) / width + 1;
-  const unsigned grid =
-      persistent_grid(resident_blocks(fit, region_chunks<W, U, F, G>, block, 0), tiles, n / W + 1, block, per_lane);
-  region_chunks<W, U><<<grid, block, 0, s>>>(n, scalar, chunk);
+  const std::size_t chunks = n / W;
+  std::size_t per = per_lane ? per_lane : 1;
+  while((chunks + block * per - 1) / (block * per) > GRID_LIMIT) per *= 2;
+  const std::size_t g = (chunks + block * per - 1) / (block * per);
+  region_chunks<W, U><<<unsigned(g ? g : 1), block, 0, s>>>(n, per, scalar, chunk);
   check(cudaGetLastError());
 }
 
 // `plan f { stage R; }`: a tile covers blockDim.x indices from `base`; `load(base, w, t, b, tile)` fills the tile
 // with the staged arrays' elements from base - R to base + b + R that lie inside them, and `body(i, base, w, tile)`
-// runs index i reading them there (runtime/cairn_exec.hpp's run_staged). With `pair`, the block holds two tiles
-// `stride` bytes apart and loads tile k + 1 into one while its lanes read tile k from the other; the barrier after
-// the lanes both publishes the next tile and frees the one just read. Without it, one tile between two barriers.
-// Every thread of a block reaches every barrier: the loop bounds depend on the block, never the thread.
-template<std::size_t R, class L, class F>
-__global__ void region_staged(std::size_t n, L load, F body, std::size_t stride, bool pair) {
-  extern __shared__ __align__(128) unsigned char tiles_smem[];
+// runs index i reading them there (runtime/cairn_exec.hpp's run_staged). Block b takes tiles b * span to
+// b * span + span - 1. Every thread of a block reaches every barrier: the loop bounds depend on the block alone.
+template<std::size_t R, class L, class F> __global__ void region_staged(std::size_t n, std::size_t span, L load, F body) {
+  extern __shared__ __align__(128) unsigned char tile_smem[];
   const std::size_t b = blockDim.x, w = b + 2 * R, t = threadIdx.x, tiles = (n + b - 1) / b;
-  std::size_t tile = blockIdx.x;
-  if(tile >= tiles) return;
-  if(!pair) {
-    for(; tile < tiles; tile += gridDim.x) {
-      const std::size_t base = tile * b;
-      __syncthreads();  // the lanes of the previous tile are done with it
-      load(base, w, t, b, tiles_smem);
-      __syncthreads();
-      if(base + t < n) body(base + t, base, w, tiles_smem);
-    }
-    return;
-  }
-  unsigned char* held = tiles_smem;
-  unsigned char* next_tile = tiles_smem + stride;
-  load(tile * b, w, t, b, held);
-  __syncthreads();
-  for(;;) {
-    const std::size_t next = tile + gridDim.x, base = tile * b;
-    if(next < tiles) load(next * b, w, t, b, next_tile);
-    if(base + t < n) body(base + t, base, w, held);
+  const std::size_t first = std::size_t(blockIdx.x) * span, last = first + span < tiles ? first + span : tiles;
+#pragma unroll 1
+  for(std::size_t tile = first; tile < last; ++tile) {
+    const std::size_t base = tile * b;
+    __syncthreads();  // the lanes of the previous tile are done with it
+    load(base, w, t, b, tile_smem);
     __syncthreads();
-    if(next >= tiles) break;
-    tile = next;
-    unsigned char* read = held;
-    held = next_tile;
-    next_tile = read;
+    if(base + t < n) body(base + t, base, w, tile_smem);
   }
 }
 
@@ -220,19 +202,17 @@ inline void start_staged(std::size_t n, L load, F body, S bytes, cudaStream_t s,
   static std::atomic<unsigned long long> fit{0};
   if(block > most) block = most;
   if(block < WARP) block = WARP;
-  const std::size_t one = (bytes(std::size_t(block) + 2 * R) + 127) / 128 * 128;
-  int optin = 0, dev = 0;
-  check(cudaGetDevice(&dev));
-  check(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-  const bool pair = 2 * one <= std::size_t(optin);
-  const std::size_t shared = pair ? 2 * one : one;
-  if(shared > std::size_t(optin)) trap();  // a tile larger than any block's shared memory
+  const std::size_t shared = bytes(std::size_t(block) + 2 * R);
   if(shared > 48 * 1024)
     check(cudaFuncSetAttribute(region_staged<R, L, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(shared)));
   const std::size_t tiles = (n + block - 1) / block;
-  const unsigned grid = persistent_grid(resident_blocks(fit, region_staged<R, L, F>, block, shared), tiles, n, block,
-                                        per_lane);
-  region_staged<R><<<grid, block, shared, s>>>(n, load, body, one, pair);
+  std::size_t span = per_lane > STAGE_TILES ? per_lane : STAGE_TILES;
+  while((tiles + span - 1) / span > GRID_LIMIT) span *= 2;
+  // a grid of at least the resident blocks (when there are tiles for them), each block `span` tiles or fewer
+  const std::size_t resident = resident_blocks(fit, region_staged<R, L, F>, block, shared);
+  const unsigned grid = region_grid(tiles, 1, span, resident);
+  const std::size_t each = (tiles + grid - 1) / grid;
+  region_staged<R><<<grid, block, shared, s>>>(n, each, load, body);
   check(cudaGetLastError());
 }
 
