@@ -538,25 +538,58 @@ class Mlp:
 
 
 def cpu_mlp_sample(budget_s: float):
-    """GFLOP/s of the oracle's restatement of derive grad's dense-layer loops (single-threaded; the reference's own
-    derive-grad output needs its compiler, which is not run here) on a reduced shape, scaled to TFLOP/s."""
+    """TFLOP/s of config 3's step on the host by the reference's own code, at a reduced shape (batch 32,
+    256 -> 1024 -> 256): its dense layers and the adjoints `derive grad` writes for them and for mse
+    (oracle/_ref/libmlp_grad.so, oracle/grad/mlp_grad.cairn through the reference's compiler; sequential f32 loops,
+    one core, the only backward the reference has), timed around those compiled calls; the relu and bf16 roundings
+    between them run in numpy outside the clock. Credited with the step's six products (the reference's adjoints
+    run each layer's forward again, which the credit leaves out). Without the reference build, the C restatement."""
     import numpy as np
 
-    from oracle import restated
+    from oracle import reference, restated
+
+    def narrow(v):  # nearest-even bf16 of finite f32 values as f32 patterns, as cr::fp::narrow rounds
+        u = np.asarray(v, np.float32).view(np.uint32).astype(np.uint64)
+        return (((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint32) << 16).view(np.float32)
 
     B, D, H, O = 32, 256, 1024, 256
     rng = np.random.default_rng(0)
-    x = rng.integers(0, 1 << 16, B * D, dtype=np.uint16) & np.uint16(0x3FFF)
-    w1 = rng.integers(0, 1 << 16, D * H, dtype=np.uint16) & np.uint16(0x3CFF)
-    w2 = rng.integers(0, 1 << 16, H * O, dtype=np.uint16) & np.uint16(0x3CFF)
+    xf = narrow(rng.standard_normal(B * D))
+    w1f = narrow(rng.standard_normal(D * H) * 0.02)
+    w2f = narrow(rng.standard_normal(H * O) * 0.02)
     t = rng.standard_normal(B * O).astype(np.float32)
+    flops_step = 2.0 * B * H * (3 * D + 3 * O)
     spent, flops = 0.0, 0.0
-    while spent < budget_s:
-        t0 = time.perf_counter()
-        restated.mlp_step(x, w1, w2, t, B, D, H, O)
-        spent += time.perf_counter() - t0
-        flops += 2.0 * B * H * (3 * D + 3 * O)
-    return flops / spent / 1e12, 1, "port", f"{int(flops / (2.0 * B * H * 6 * D))} steps at batch 32, 256 -> 1024 -> 256"
+    if reference.grad_available():
+
+        while spent < budget_s:
+            t0 = time.perf_counter()
+            pre = reference.dense(xf, w1f, B, D, H)
+            spent += time.perf_counter() - t0
+            hf = narrow(np.maximum(pre, 0))
+            t0 = time.perf_counter()
+            y = reference.dense(hf, w2f, B, H, O)
+            _, dyf = reference.mse_grad(y, t)
+            spent += time.perf_counter() - t0
+            dy = narrow(dyf)
+            t0 = time.perf_counter()
+            dh_pre, _ = reference.dense_grad(hf, w2f, dy, B, H, O)
+            spent += time.perf_counter() - t0
+            dh = narrow(np.where(pre > 0, dh_pre, np.float32(0)))
+            t0 = time.perf_counter()
+            reference.dense_grad(xf, w1f, dh, B, D, H)
+            spent += time.perf_counter() - t0
+            flops += flops_step
+        kind = "reference"
+    else:
+        bits = [(v.view(np.uint32) >> 16).astype(np.uint16) for v in (xf, w1f, w2f)]
+        while spent < budget_s:
+            t0 = time.perf_counter()
+            restated.mlp_step(*bits, t, B, D, H, O)
+            spent += time.perf_counter() - t0
+            flops += flops_step
+        kind = "port"
+    return flops / spent / 1e12, 1, kind, f"{int(flops / flops_step)} steps at batch 32, 256 -> 1024 -> 256"
 
 
 # ---------------------------------------------------------------------------------------------------------------------

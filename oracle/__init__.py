@@ -6,7 +6,9 @@ and only as the checker or the timed CPU baseline; the cairn_b200 package never 
   restated   numpy wrappers of liboracle.so, the C restatement in cairn_oracle.c (each function cites the
              reference file:line it restates)
   reference  numpy wrappers of _ref/libcairn_ref.so, the reference's own header-only host path compiled from its
-             sources by the Makefile here (present where the reference tree was available at build time)
+             sources by the Makefile here, and of _ref/libmlp_grad.so, grad/mlp_grad.cairn built by the reference's
+             own compiler (its `derive grad` output for config 3's layers); both present where the reference tree
+             was available at build time
   exact_sum_f32_bits  a pure-Python model of the correctly rounded sum (Fraction arithmetic) for small cases
 """
 
@@ -24,16 +26,44 @@ import numpy as np
 HERE = Path(__file__).resolve().parent
 RESTATED = HERE / "liboracle.so"
 REFERENCE = HERE / "_ref" / "libcairn_ref.so"
+GRAD = HERE / "_ref" / "libmlp_grad.so"
+GRAD_SOURCE = HERE / "grad" / "mlp_grad.cairn"
 
 _z, _p, _f = C.c_size_t, C.c_void_p, C.c_float
 
 
-def build(reference_runtime: str | None = None) -> None:
-    """make -C oracle [REF=...]: the restatement always, the reference's host path when its runtime dir is given."""
+def build(reference_tree: str | None = None) -> None:
+    """make -C oracle [REF=...]: the restatement always; where the CAIRN reference checkout (the directory holding
+    src/cairn) is given, also the reference's host path from its runtime headers, and grad/mlp_grad.cairn through the
+    reference's own compiler (`cairn build --kind library --cxx g++`, its host toolchain's flags)."""
     cmd = ["make", "-s", "-C", str(HERE)]
-    if reference_runtime:
-        cmd.append(f"REF={reference_runtime}")
+    if reference_tree:
+        cmd.append(f"REF={Path(reference_tree) / 'src' / 'cairn' / 'runtime'}")
     subprocess.run(cmd, check=True)
+    if reference_tree:
+        build_grad(reference_tree)
+
+
+def build_grad(reference_tree: str) -> Path:
+    """grad/mlp_grad.cairn compiled by the reference's compiler into _ref/libmlp_grad.so (and its C header)."""
+    import json
+    import os
+    import shutil
+    import sys
+    import tempfile
+
+    env = dict(os.environ, PYTHONPATH=str(Path(reference_tree) / "src"))
+    with tempfile.TemporaryDirectory(prefix="cairn-grad-") as tmp:
+        done = subprocess.run([sys.executable, "-m", "cairn", "build", str(GRAD_SOURCE), "--cxx", "g++", "--kind",
+                               "library", "--header", "--out", tmp, "--format", "json"], capture_output=True, text=True,
+                              env=env, cwd=tmp, timeout=900)
+        if done.returncode != 0:
+            raise RuntimeError(f"cairn build mlp_grad.cairn failed:\n{done.stdout[-3000:]}{done.stderr[-3000:]}")
+        record = json.loads(done.stdout)
+        GRAD.parent.mkdir(exist_ok=True)
+        shutil.copy2(record["artifact"], GRAD)
+        shutil.copy2(record["header"], GRAD.with_name("mlp_grad.h"))
+    return GRAD
 
 
 def _ptr(a: np.ndarray) -> int:
@@ -65,6 +95,7 @@ class _Lib:
 
 _rest = _Lib(RESTATED, "oracle_")
 _ref = _Lib(REFERENCE, "ref_")
+_grad = _Lib(GRAD, "cf_")
 
 MMA_DTYPES = {"bf16": np.uint16, "f16": np.uint16, "f8e4m3": np.uint8, "f8e5m2": np.uint8, "f32": np.float32}
 
@@ -247,6 +278,80 @@ class reference:
     @staticmethod
     def lanes() -> int:
         return int(_ref.fn("lanes", _z, [])())
+
+    # ---- derive grad (_ref/libmlp_grad.so: grad/mlp_grad.cairn through the reference's compiler) ----
+    @staticmethod
+    def grad_available() -> bool:
+        return _grad.available()
+
+    @staticmethod
+    def dense(x: np.ndarray, w: np.ndarray, b: int, k: int, n: int) -> np.ndarray:
+        """cf_dense: out (b x n) = x (b x k) w (k x n) in f32, each output's terms summed in increasing p."""
+        x, w = np.ascontiguousarray(x, np.float32), np.ascontiguousarray(w, np.float32)
+        out = np.empty(b * n, np.float32)
+        _grad.fn("dense", None, [_z, _z, _z, _z, _p, _z, _p, _z, _p])(b, k, n, b * k, _ptr(x), k * n, _ptr(w), b * n,
+                                                                      _ptr(out))
+        return out
+
+    @staticmethod
+    def dense_grad(x: np.ndarray, w: np.ndarray, d_out: np.ndarray, b: int, k: int, n: int):
+        """cf_dense_grad, derive grad's adjoint of `dense`, from zeroed adjoints: returns (d_x, d_w)."""
+        x, w = np.ascontiguousarray(x, np.float32), np.ascontiguousarray(w, np.float32)
+        d_out = np.ascontiguousarray(d_out, np.float32)
+        out, d_x, d_w = np.empty(b * n, np.float32), np.zeros(b * k, np.float32), np.zeros(k * n, np.float32)
+        _grad.fn("dense_grad", None, [_z, _z, _z, _z, _p, _z, _p, _z, _p, _p, _p, _p])(
+            b, k, n, b * k, _ptr(x), k * n, _ptr(w), b * n, _ptr(out), _ptr(d_x), _ptr(d_w), _ptr(d_out))
+        return d_x, d_w
+
+    @staticmethod
+    def mse_grad(y: np.ndarray, t: np.ndarray, seed: float = 1.0):
+        """cf_mse_grad from a zeroed adjoint: returns (the loss, d_y)."""
+        y, t = np.ascontiguousarray(y, np.float32), np.ascontiguousarray(t, np.float32)
+        d_y = np.zeros(y.size, np.float32)
+        loss = _grad.fn("mse_grad", _f, [_z, _p, _p, _f, _p])(y.size, _ptr(y), _ptr(t), seed, _ptr(d_y))
+        return np.float32(loss), d_y
+
+    @staticmethod
+    def relu(z: np.ndarray) -> np.ndarray:
+        f = _grad.fn("relu", _f, [_f])
+        return np.array([f(float(v)) for v in np.asarray(z, np.float32).ravel()], np.float32)
+
+    @staticmethod
+    def relu_grad(z: np.ndarray, seed: np.ndarray) -> np.ndarray:
+        """cf_relu_grad per element from a zeroed adjoint: d_z = seed where z > 0, else 0."""
+        f = _grad.fn("relu_grad", _f, [_f, _f, C.POINTER(C.c_float)])
+        out = np.zeros(np.asarray(z).size, np.float32)
+        cell = C.c_float(0.0)
+        for i, (zv, sv) in enumerate(zip(np.asarray(z, np.float32).ravel(), np.asarray(seed, np.float32).ravel())):
+            cell.value = 0.0
+            f(float(zv), float(sv), C.byref(cell))
+            out[i] = cell.value
+        return out
+
+    @staticmethod
+    def narrow_bf16_array(x: np.ndarray) -> np.ndarray:
+        f = _ref.fn("narrow_bf16", C.c_uint16, [C.c_double])
+        return np.array([f(float(v)) for v in np.asarray(x, np.float32).ravel()], np.uint16)
+
+    @staticmethod
+    def mlp_step(x: np.ndarray, w1: np.ndarray, w2: np.ndarray, t: np.ndarray, B: int, D: int, Hd: int, O: int):
+        """Config 3's step from the reference's own code alone: its dense layers and derive-grad adjoints
+        (_ref/libmlp_grad.so), its relu and relu_grad, its mse_grad, and cr::fp::narrow to bf16 where the step
+        stores bf16 (H, dY, dH). x, w1, w2 are bf16 patterns, t f32. Returns the same dict as restated.mlp_step."""
+        xf = reference.widen("bf16", x)
+        w1f = reference.widen("bf16", w1)
+        w2f = reference.widen("bf16", w2)
+        pre = reference.dense(xf, w1f, B, D, Hd)
+        h = reference.narrow_bf16_array(reference.relu(pre))
+        hf = reference.widen("bf16", h)
+        y = reference.dense(hf, w2f, B, Hd, O)
+        loss, dy_f32 = reference.mse_grad(y, t)
+        dy = reference.narrow_bf16_array(dy_f32)
+        dh_pre, dw2 = reference.dense_grad(hf, w2f, reference.widen("bf16", dy), B, Hd, O)
+        dh = reference.narrow_bf16_array(reference.relu_grad(pre, dh_pre))
+        dx, dw1 = reference.dense_grad(xf, w1f, reference.widen("bf16", dh), B, D, Hd)
+        return {"H": h, "Y": y, "dY": dy, "loss": np.asarray([loss], np.float32), "dW2": dw2, "dH": dh,
+                "dW1": dw1, "dX": dx}
 
 
 # ---- a pure-Python model of the correctly rounded f32 sum (for small cases) ----------------------------------------

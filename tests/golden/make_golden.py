@@ -1,7 +1,7 @@
 """Writes tests/golden/*.npz: inputs and the outputs of the CAIRN reference's own host path on them.
 
-Run where the reference's host path is built (oracle/_ref/libcairn_ref.so, compiled from the reference's runtime
-headers by oracle/Makefile):  python tests/golden/make_golden.py
+Run where the reference's host path is built (oracle/_ref, by oracle.build with the CAIRN reference checkout):
+    python tests/golden/make_golden.py [NAME ...]        (every fixture, or the named ones)
 
 The fixtures pin oracle/cairn_oracle.c (tests/test_oracle.py) on machines that have no reference tree, such as the
 GPU box, and give the GPU parity tests the reference's own answers for the cases of its tests:
@@ -12,9 +12,15 @@ GPU box, and give the GPU parity tests the reference's own answers for the cases
   u64.npz    cr::par::reduce over cr::Sum<u64> on tests/inputs.py's u64_cases: data[i] = i for n = 1e6 (BASELINE
              config 1) and overflow cases
   saxpy.npz  cr::par::run of out = a * x + y
-  f32gemm.npz  the `parallel e in m*n` f32 GEMM region of BASELINE config 1, at a reduced size
+  f32gemm.npz  the `parallel e in m*n` f32 GEMM region of BASELINE config 1 at its size, M = N = K = 512, with
+             A then B drawn U[-1, 1] from numpy's default_rng(0) (the test draws them again; the first values are
+             kept to show the stream has not changed); a 96^3 case with its inputs stored
   scan.npz   cr::par::scan: inclusive add_wrap over u32 and exclusive max over i32, on sizes around the device
              scan's tiles (4096 four-byte elements) and with wrapping totals
+  mlp_grad.npz  BASELINE config 3's step at a reduced shape (batch 32, 128 -> 512 -> 128) from the reference's own
+             code: oracle/grad/mlp_grad.cairn built by the reference's compiler (its dense layer and the adjoints
+             `derive grad` writes for it, relu and mse with theirs; oracle/_ref/libmlp_grad.so), chained as a CAIRN
+             program would chain them, with cr::fp::narrow to bf16 where the step stores bf16 (H, dY, dH)
 """
 
 from __future__ import annotations
@@ -79,7 +85,11 @@ def f32gemm() -> dict:
     a = rng.uniform(-1, 1, m * k).astype(np.float32)
     b = rng.uniform(-1, 1, k * n).astype(np.float32)
     c = np.zeros(m * n, np.float32)
-    return {"a": a, "b": b, "shape": np.asarray([m, n, k]), "want": reference.gemm_f32_region(c, a, b, m, n, k)}
+    out = {"a": a, "b": b, "shape": np.asarray([m, n, k]), "want": reference.gemm_f32_region(c, a, b, m, n, k)}
+    a512, b512 = inputs.config1_gemm()
+    out["512/want"] = reference.gemm_f32_region(np.zeros(512 * 512, np.float32), a512, b512, 512, 512, 512)
+    out["512/first"] = np.concatenate([a512[:4], b512[:4]])
+    return out
 
 
 SCAN_SIZES = (1, 2, 4095, 4096, 4097, 8193)
@@ -98,11 +108,24 @@ def scan() -> dict:
     return out
 
 
+def mlp_grad() -> dict:
+    B, D, H, O = inputs.MLP_GOLDEN_SHAPE
+    x, w1, w2, t = inputs.mlp_case(B, D, H, O, seed=33)
+    out = {"x": x, "w1": w1, "w2": w2, "t": t, "shape": np.asarray([B, D, H, O])}
+    for key, v in reference.mlp_step(x, w1, w2, t, B, D, H, O).items():
+        out[f"want/{key}"] = v
+    return out
+
+
 def main() -> None:
-    if not reference.available():
-        raise SystemExit("oracle/_ref/libcairn_ref.so is not built: make -C oracle REF=<cairn>/src/cairn/runtime")
+    if not reference.available() or not reference.grad_available():
+        raise SystemExit("oracle/_ref is not built: CAIRN_REFERENCE=<cairn checkout> python -c "
+                         "'import __graft_entry__ as g; g.build()'")
+    only = set(sys.argv[1:])
     for name, fn in (("mma", mma), ("sum", sums), ("u64", u64), ("saxpy", saxpy), ("f32gemm", f32gemm),
-                     ("scan", scan)):
+                     ("scan", scan), ("mlp_grad", mlp_grad)):
+        if only and name not in only:
+            continue
         np.savez_compressed(HERE / f"{name}.npz", **fn())
         print(f"wrote {name}.npz")
 

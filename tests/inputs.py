@@ -168,3 +168,26 @@ def u64_cases() -> dict[str, np.ndarray]:
 def saxpy_case(n: int, seed: int = 0):
     rng = np.random.default_rng(seed)
     return rng.uniform(-1, 1, n).astype(np.float32), rng.uniform(-1, 1, n).astype(np.float32), np.float32(2.5)
+
+
+# BASELINE config 3 at the reduced shape of tests/golden/mlp_grad.npz: batch 32, 128 -> 512 -> 128.
+MLP_GOLDEN_SHAPE = (32, 128, 512, 128)
+
+
+def mlp_case(B: int, D: int, H: int, O: int, seed: int = 0):
+    """Config 3's operands at any shape: x ~ N(0, 1) and w1, w2 ~ N(0, 0.32) as bf16 patterns (config 3's N(0, 0.02)
+    scaled by 16, so that products of a few hundred terms keep a spread of signs and sizes), target t ~ N(0, 1)."""
+    rng = np.random.default_rng(seed)
+    x = encode("bf16", rng.standard_normal(B * D))
+    w1 = encode("bf16", rng.standard_normal(D * H) * 0.02 * 16)
+    w2 = encode("bf16", rng.standard_normal(H * O) * 0.02 * 16)
+    t = rng.standard_normal(B * O).astype(np.float32)
+    return x, w1, w2, t
+
+
+def config1_gemm():
+    """BASELINE config 1's f32 GEMM operands: M = N = K = 512, A then B ~ U[-1, 1] from numpy's default_rng(0)."""
+    rng = np.random.default_rng(0)
+    a = rng.uniform(-1, 1, 512 * 512).astype(np.float32)
+    b = rng.uniform(-1, 1, 512 * 512).astype(np.float32)
+    return a, b

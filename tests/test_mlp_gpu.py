@@ -1,9 +1,14 @@
-"""BASELINE config 3, the 2-layer MLP forward + backward, on the B200 against the oracle's restatement of derive
-grad's dense-layer loops (oracle_mlp_step), at reduced shapes the oracle finishes in seconds, and against torch's
-own f32 autograd as a second reference. The bf16 intermediates (H, dY, dH) are stored as the oracle stores them;
-results agree within the north star's bf16 tolerance (Frobenius 2e-2), and in practice to about 1e-3."""
+"""BASELINE config 3, the 2-layer MLP forward + backward, on the B200: against the reference's own `derive grad`
+output (tests/golden/mlp_grad.npz: oracle/grad/mlp_grad.cairn built by the reference's compiler, its dense layers and
+their adjoints chained with relu_grad, mse_grad and cr::fp::narrow), against the oracle's restatement of those loops
+(oracle_mlp_step, pinned bit for bit to the same fixture by tests/test_oracle.py) at larger reduced shapes, and
+against torch's own f32 autograd as a third reference. The bf16 intermediates (H, dY, dH) are stored as the
+reference stores them; results agree within the north star's bf16 tolerance (Frobenius 2e-2), and in practice to
+about 1e-3."""
 
 from __future__ import annotations
+
+from pathlib import Path
 
 import numpy as np
 import pytest
@@ -15,6 +20,7 @@ from cairn_b200 import mlp
 from oracle import restated
 
 pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
 def _rel(a, b) -> float:
@@ -25,6 +31,32 @@ def _rel(a, b) -> float:
 
 def _bits(t: torch.Tensor) -> np.ndarray:
     return t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16).ravel()
+
+
+def test_mlp_step_against_the_reference_derive_grad(cuda):
+    """The device step on the fixture's operands against the reference's derive-grad chain: H within one bf16
+    rounding plus the multiply's contract bound of the reference's f32 sums, element by element; the ReLU mask
+    exactly where H > 0; every other tensor within Frobenius 2e-2; the loss within 1e-3."""
+    d = np.load(GOLDEN / "mlp_grad.npz")
+    B, D, H, O = map(int, d["shape"])
+    x, w1, w2, t = d["x"], d["w1"], d["w2"], d["t"]
+    dev = lambda bits, shape: torch.from_numpy(bits.view(np.int16).copy()).to(cuda).view(torch.bfloat16).view(shape)
+    ws = mlp.mlp_step(dev(x, (B, D)), dev(w1, (D, H)), dev(w2, (H, O)), torch.from_numpy(t).to(cuda).view(B, O))
+    cairn_b200.stream_status()
+    want_h = inputs.decode("bf16", d["want/H"])
+    got_h = inputs.decode("bf16", _bits(ws.h))
+    mag = np.abs(inputs.decode("bf16", x).reshape(B, D)) @ np.abs(inputs.decode("bf16", w1).reshape(D, H))
+    tol = 2.0**-8 * np.abs(want_h) + 2 * (D + 1) * 2.0**-22 * mag.ravel()
+    assert (np.abs(got_h - want_h) <= tol).all()
+    assert _rel(ws.y.cpu().numpy(), d["want/Y"]) < 2e-2
+    assert _rel(inputs.decode("bf16", _bits(ws.dy)), inputs.decode("bf16", d["want/dY"])) < 2e-2
+    for name in ("dW2", "dW1", "dX"):
+        assert _rel(getattr(ws, name.lower()).cpu().numpy(), d[f"want/{name}"]) < 2e-2, name
+    got_dh = inputs.decode("bf16", _bits(ws.dh))
+    assert _rel(got_dh, inputs.decode("bf16", d["want/dH"])) < 2e-2
+    assert (got_dh[got_h <= 0] == 0).all()
+    want_loss = float(d["want/loss"][0])
+    assert abs(float(ws.loss.item()) - want_loss) <= 1e-3 * abs(want_loss)
 
 
 @pytest.mark.parametrize("B,D,H,O", [(128, 256, 512, 128), (264, 136, 392, 200), (512, 512, 1024, 512)])

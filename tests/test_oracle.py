@@ -1,7 +1,8 @@
 """Pins the CPU oracle (oracle/cairn_oracle.c) before any GPU result is judged against it.
 
 1. Against the golden fixtures (tests/golden/*.npz), which hold the CAIRN reference's own host path's outputs
-   (cr::tensor::multiply, cr::par::sum, cr::par::reduce over cr::Sum, cr::par::run): bit for bit. Runs anywhere.
+   (cr::tensor::multiply, cr::par::sum, cr::par::reduce over cr::Sum, cr::par::run, and config 3's step from the
+   reference compiler's `derive grad` output): bit for bit. Runs anywhere.
 2. Against the reference's host path live (oracle/_ref, built from the reference's headers where its source tree
    exists): bit for bit on fresh seeded inputs.
 3. The exact sum against an independent rational model (Fraction arithmetic) on the rounding-boundary cases.
@@ -76,6 +77,54 @@ def test_restated_f32_region_gemm_equals_the_reference_fixture():
     m, n, k = map(int, d["shape"])
     got = restated.mma("f32", np.zeros(m * n, np.float32), d["a"], d["b"], m, n, k)
     assert np.array_equal(got.view(np.uint32), d["want"].view(np.uint32))
+
+
+def test_restated_f32_region_gemm_at_config_1_size():
+    """M = N = K = 512, A and B ~ U[-1, 1] from seed 0, against the reference's region."""
+    d = np.load(GOLDEN / "f32gemm.npz")
+    a, b = inputs.config1_gemm()
+    assert np.array_equal(np.concatenate([a[:4], b[:4]]).view(np.uint32), d["512/first"].view(np.uint32))
+    got = restated.mma("f32", np.zeros(512 * 512, np.float32), a, b, 512, 512, 512)
+    assert np.array_equal(got.view(np.uint32), d["512/want"].view(np.uint32))
+
+
+MLP_KEYS = ("H", "Y", "dY", "dW2", "dH", "dW1", "dX")
+
+
+def _mlp_loss_bound(want_loss: float, m: int) -> float:
+    """The reference sums the m squares in f32 in index order (mse, a host `reduce +` over `for`); the step and the
+    restatement sum them exactly in f64 and round once. Both lie within (m + 1) 2^-24 of the exact mean."""
+    return 2 * (m + 1) * 2.0**-24 * abs(want_loss)
+
+
+def test_restated_mlp_step_equals_the_reference_derive_grad_fixture():
+    """Config 3's step at a reduced shape against the reference's own code: the dense layers and the adjoints its
+    `derive grad` writes (oracle/grad/mlp_grad.cairn through the reference's compiler), relu_grad, mse_grad and
+    cr::fp::narrow (tests/golden/mlp_grad.npz). Every tensor bit for bit; the loss within the f32 sum's bound."""
+    d = np.load(GOLDEN / "mlp_grad.npz")
+    B, D, H, O = map(int, d["shape"])
+    got = restated.mlp_step(d["x"], d["w1"], d["w2"], d["t"], B, D, H, O)
+    for key in MLP_KEYS:
+        a, w = np.asarray(got[key]), np.asarray(d[f"want/{key}"])
+        assert a.dtype == w.dtype and np.array_equal(a.view(np.uint8), w.view(np.uint8)), key
+    want_loss = float(d["want/loss"][0])
+    assert abs(float(got["loss"][0]) - want_loss) <= _mlp_loss_bound(want_loss, B * O)
+
+
+@pytest.mark.skipif(not reference.grad_available(), reason="oracle/_ref/libmlp_grad.so is not built here")
+def test_the_reference_derive_grad_chain_live():
+    """The reference's derive-grad chain run now gives the fixture again, and agrees with the restatement on a
+    second shape and seed."""
+    d = np.load(GOLDEN / "mlp_grad.npz")
+    B, D, H, O = map(int, d["shape"])
+    live = reference.mlp_step(d["x"], d["w1"], d["w2"], d["t"], B, D, H, O)
+    for key in (*MLP_KEYS, "loss"):
+        assert np.array_equal(np.asarray(live[key]).view(np.uint8), np.asarray(d[f"want/{key}"]).view(np.uint8)), key
+    B, D, H, O = 12, 40, 72, 24
+    x, w1, w2, t = inputs.mlp_case(B, D, H, O, seed=5)
+    ref, rest = reference.mlp_step(x, w1, w2, t, B, D, H, O), restated.mlp_step(x, w1, w2, t, B, D, H, O)
+    for key in MLP_KEYS:
+        assert np.array_equal(np.asarray(ref[key]).view(np.uint8), np.asarray(rest[key]).view(np.uint8)), key
 
 
 def test_the_exact_sum_matches_an_independent_rational_model():
