@@ -328,25 +328,27 @@ class Gemm:
 
     def e2e(self, steps: int, warmup: int):
         """The same product from pinned host memory through cairn_b200.HostGemm (the library's host-buffer multiply:
-        B, bias and A's row chunks copied in, each chunk's rows of C computed as they land and copied back), every
-        step's operands in and its whole bf16 (or f32) result out; steps overlap as a stream of products would."""
+        A's row chunks copied in, each chunk's rows of C computed as they land and copied back), every step's A in
+        and its whole bf16 (or f32) result out; B and the bias stay resident on the device, as a layer's weights do
+        from step to step. Steps overlap as a stream of products would. Also returns each GPU's host-link rates."""
         torch = self.torch
         from cairn_b200 import HostGemm
 
         a_h = [self.a[s].cpu().pin_memory() for s in range(2)]
-        b_h = self.b[0].cpu().pin_memory()
-        bias_h = None if self.config5 else self.bias.cpu().pin_memory()
         out_h = torch.empty(self.out[0].shape, dtype=self.out[0].dtype).pin_memory()
         hg = HostGemm(self.m, self.n, self.k, out_dtype=self.out[0].dtype, bias=not self.config5,
                       device=self.dist.device)
+        bias = None if self.config5 else self.bias
 
         def step(i):
-            done = hg.submit(a_h[i % 2], b_h, out_h, bias_h, relu=not self.config5)
+            done = hg.submit(a_h[i % 2], self.b[0], out_h, bias, relu=not self.config5)
             self.stream.wait_event(done)  # the timed region ends when the last result is in host memory
 
         ms, _, _, _ = time_steps(self.dist, self.stream, step, steps, warmup, per_launch=False)
-        h2d = a_h[0].numel() * 2 + b_h.numel() * 2 + (bias_h.numel() * 4 if bias_h is not None else 0)
+        h2d = a_h[0].numel() * 2
         d2h = out_h.numel() * out_h.element_size()
+        self.link = {"h2d_GBps_per_gpu": h2d / (ms * 1e-3) / 1e9, "d2h_GBps_per_gpu": d2h / (ms * 1e-3) / 1e9,
+                     "resident": "B and the bias (uploaded once, as weights are)"}
         return self.dist.world * self.flops / (ms * 1e-3) / 1e12, h2d, d2h
 
 
@@ -592,6 +594,41 @@ def cpu_mlp_sample(budget_s: float):
     return flops / spent / 1e12, 1, kind, f"{int(flops / flops_step)} steps at batch 32, 256 -> 1024 -> 256"
 
 
+def scaling_legs(dist: Dist) -> dict:
+    """The sharded designs of BASELINE configs 5 and 4, run by every rank after the headline at every N so that the
+    scaling run records them: config 5's M-sharded product (M = 65536 split into N row blocks, N = K = 8192, f32 out;
+    strong scaling, no collective) with its optional all-gather of C timed apart, and the range-sharded f32 and u64
+    sums over n = 2^30 with their all-gather of the ranks' parts inside each step. Times are device times, the max
+    over ranks (CUDA events between barriers, as the headline's)."""
+    import torch
+
+    from cairn_b200 import shard
+
+    out: dict = {}
+    g5 = Gemm(dist, config5=True)
+    ms, launch_ms, _, _ = time_steps(dist, g5.stream, g5.launch, 5, 3)
+    out["config5"] = {"rows_per_gpu": g5.m, "ms_per_product": ms, "TFLOP/s": dist.world * g5.flops / (ms * 1e-3) / 1e12,
+                      "per_gpu_TFLOP/s": g5.flops / (launch_ms * 1e-3) / 1e12, "scaling": "strong"}
+    if dist.world > 1:
+        whole = torch.empty(g5.m_total, g5.n, dtype=torch.float32, device=dist.device)
+        gms, _, _, _ = time_steps(dist, g5.stream, lambda i: shard.gather_rows(g5.out[0], g5.m_total, out=whole), 3, 1)
+        received = (g5.m_total - g5.m) * g5.n * 4
+        out["config5"]["allgather_ms"] = gms
+        out["config5"]["allgather_GBps_per_gpu"] = received / (gms * 1e-3) / 1e9
+        out["config5"]["allgather_note"] = "NCCL all-gather of the f32 C row blocks, received bytes per GPU"
+        del whole
+    del g5
+    torch.cuda.empty_cache()
+    for w in ("sum_f32", "sum_u64"):
+        st = Stream(dist, w, 30)
+        ms, _, _, _ = time_steps(dist, st.stream, st.launch, 10, 3)
+        out[w] = {"n": st.n_total, "ms_per_step": ms, "GB/s": st.n_total * st.bytes / (ms * 1e-3) / 1e9,
+                  "scaling": "strong", "exchange": "parts all-gathered every step" if dist.world > 1 else "none"}
+        del st
+        torch.cuda.empty_cache()
+    return out
+
+
 # ---------------------------------------------------------------------------------------------------------------------
 REF_DEVICE = ROOT / "baseline" / "_ref" / "libhotpath_ref.so"
 
@@ -786,6 +823,8 @@ def main() -> None:
     ap.add_argument("--log2n", type=int, default=30, help="saxpy/sum size 2^log2n (BASELINE: 30; smaller for ncu)")
     ap.add_argument("--no-reference-device", action="store_true",
                     help="skip the drop-in legs (the emitted program on both machines, timed in subprocesses)")
+    ap.add_argument("--no-scaling-legs", action="store_true",
+                    help="skip the default line's config-5 and sharded-sum legs (run at every N)")
     ap.add_argument("--machine-measure", default=None, help=argparse.SUPPRESS)  # that subprocess
     args = ap.parse_args()
     if args.machine_measure:
@@ -869,30 +908,40 @@ def main() -> None:
     refdev = dropin = None
     if dist.rank == 0 and dist.world == 1 and not args.no_reference_device:
         dropin, refdev = dropin_report(args)
-
+    link = getattr(wl, "link", None)
     launches = args.steps * (7 if isinstance(wl, Mlp) else 2 if isinstance(wl, Scan) else
                              1 if isinstance(wl, Gemm) or args.workload != "sum_f32" or dist.world == 1 else 2)
+    scaling_kind = wl.scaling if isinstance(wl, (Gemm, Mlp, Scan)) else "strong"
+    long_step = isinstance(wl, Mlp) or args.workload == "gemm5"
+    scaling = None
+    if args.workload == "gemm" and not args.no_scaling_legs:
+        del wl
+        torch.cuda.empty_cache()
+        scaling = scaling_legs(dist)
+
     line = {
         "metric": BASELINE_METRIC, "value": value, "unit": unit, "n_gpus": dist.world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-        "scaling": wl.scaling if isinstance(wl, (Gemm, Mlp, Scan)) else "strong", "vs_baseline": None,
+        "scaling": scaling_kind, "vs_baseline": None,
         "dtype": dtype,
         "data": "synthetic (seeded device generators; random-init operands of the configs' shapes and distributions)",
         "config": config_of(args, dist),
         "roofline": {"bound": bound, "kernel": kernel, "achieved": achieved, "peak": peak, "unit": unit,
                      "frac": achieved / peak,
-                     "peak_source": f"{peak_source} ({'hbm_gbs' if bound == 'hbm' else ('bf16_tflops_sustained: a long step' if isinstance(wl, Mlp) or args.workload == 'gemm5' else 'bf16_tflops burst')})",
+                     "peak_source": f"{peak_source} ({'hbm_gbs' if bound == 'hbm' else ('bf16_tflops_sustained: a long step' if long_step else 'bf16_tflops burst')})",
                      "traffic": traffic},
         "cpu_baseline": cpu,
         "reference_on_b200": refdev,
         "dropin_machines": dropin,
         "clocks": clocks,
-        "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+        "e2e": {"value": e2e_val, "unit": unit, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                **({"link": link} if link else {})},
         "gpu_launches": launches,
     }
+    if scaling is not None:
+        line["scaling_legs"] = scaling
     if dist.rank == 0:
         print(json.dumps(line), flush=True)
-    del wl
     torch.cuda.synchronize()
     dist.close()
 

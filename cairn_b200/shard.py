@@ -3,7 +3,9 @@
 The reference is single-GPU (no collective anywhere in its runtime); the sharded forms follow the partition its
 operations allow:
   row_block / sharded_gemm   the multiply split into contiguous row blocks of A and C, B replicated: every rank
-                             computes its block with no exchange (rows are independent in mma_unordered's contract).
+                             computes its block with no exchange (rows are independent in mma_unordered's contract);
+                             with gather=True, one NCCL all-gather then gives every rank the whole C (gather_rows),
+                             the one collective the product's partition ever needs.
   range_of / sharded_saxpy   contiguous index ranges of a `parallel` region: no exchange.
   sharded_sum_f32            each rank reduces its range to a part (the double-double total and the special-value
                              flags, cairn_b200_sum_f32_partial); one all-gather of 24 bytes per rank; every rank
@@ -28,7 +30,7 @@ from datetime import timedelta
 import torch
 import torch.distributed as dist
 
-from ._lib import ERR_OVERFLOW, ERR_TIMEOUT, CairnError, check, lib
+from ._lib import ERR_OVERFLOW, ERR_SHAPE, ERR_TIMEOUT, CairnError, check, lib
 from .ops import gemm, reduce_sum, saxpy
 
 
@@ -42,9 +44,45 @@ def row_block(m: int, world: int, rank: int) -> tuple[int, int]:
     return range_of(m, world, rank)
 
 
-def sharded_gemm(a_block: torch.Tensor, b: torch.Tensor, **kw) -> torch.Tensor:
-    """This rank's row block of op(A) * op(B): no communication."""
-    return gemm(a_block, b, **kw)
+def gather_rows(block: torch.Tensor, m: int, group=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """Every rank's row block (row_block's partition of m rows, rank order) gathered into the whole m-row matrix on
+    every rank, by one NCCL all-gather. When the blocks are equal (m divisible by the world size) they land straight
+    in `out`; otherwise each block is padded to the largest, gathered, and the padding dropped. A peer that never
+    joins ends the call with CairnError(ERR_TIMEOUT) after the process group's timeout."""
+    world, rank = dist.get_world_size(group), dist.get_rank(group)
+    lo, hi = row_block(m, world, rank)
+    if block.shape[0] != hi - lo:
+        raise CairnError(ERR_SHAPE, f"gather_rows: rank {rank} holds {block.shape[0]} rows, its block is {hi - lo}")
+    rest = tuple(block.shape[1:])
+    if out is None:
+        out = torch.empty((m, *rest), dtype=block.dtype, device=block.device)
+    elif tuple(out.shape) != (m, *rest) or out.dtype != block.dtype or not out.is_contiguous():
+        raise CairnError(ERR_SHAPE, "gather_rows: out is the whole contiguous matrix of the blocks' type")
+    block = block.contiguous()
+    if m % world == 0:
+        _all_gather(out.view(-1), block.view(-1), group, "gather_rows")
+        return out
+    tall = -(-m // world)
+    padded = torch.zeros((tall, *rest), dtype=block.dtype, device=block.device)
+    padded[: hi - lo].copy_(block)
+    flat = torch.empty((world * tall, *rest), dtype=block.dtype, device=block.device)
+    _all_gather(flat.view(-1), padded.view(-1), group, "gather_rows")
+    for r in range(world):
+        r0, r1 = row_block(m, world, r)
+        out[r0:r1].copy_(flat[r * tall: r * tall + (r1 - r0)])
+    return out
+
+
+def sharded_gemm(a_block: torch.Tensor, b: torch.Tensor, *, gather: bool = False, m: int | None = None, group=None,
+                 **kw) -> torch.Tensor:
+    """This rank's row block of op(A) * op(B), with no communication; with gather=True, the whole product on every
+    rank (gather_rows over the m rows of A, m defaulting to the sum of the ranks' blocks at equal sizes)."""
+    block = gemm(a_block, b, **kw)
+    if not gather:
+        return block
+    if m is None:
+        m = block.shape[0] * dist.get_world_size(group)
+    return gather_rows(block, m, group)
 
 
 def sharded_saxpy(a: float, x_local: torch.Tensor, y_local: torch.Tensor, out_local: torch.Tensor | None = None):

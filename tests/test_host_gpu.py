@@ -49,6 +49,27 @@ def test_calls_in_flight_each_match_the_oracle(cuda):
         assert (np.abs(out.numpy() - want) <= _bound(a, cases[0][1], m, n, k)).all()
 
 
+def test_resident_weights_give_the_same_bits_as_weights_from_host(cuda):
+    """B and the bias as device tensors kept from call to call (a layer's weights): only A crosses in, and each
+    result equals, bit for bit, the same call with B and the bias copied in from host memory."""
+    m, n, k = 768, 512, 384
+    hg = cairn_b200.HostGemm(m, n, k, bias=True, device=cuda, chunks=2, depth=2)
+    cases = [_case(m, n, k, seed) for seed in (11, 12)]
+    b_bits, bias = cases[0][1], cases[0][2]
+    b_dev = _host(b_bits, (k, n)).to(cuda)
+    bias_dev = torch.from_numpy(bias).to(cuda)
+    for a, _, _ in cases:
+        resident = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+        copied = torch.empty((m, n), dtype=torch.bfloat16).pin_memory()
+        hg.submit(_host(a, (m, k)), b_dev, resident, bias_dev, relu=True).synchronize()
+        hg.submit(_host(a, (m, k)), _host(b_bits, (k, n)), copied, torch.from_numpy(bias).pin_memory(),
+                  relu=True).synchronize()
+        assert torch.equal(resident.view(torch.int16), copied.view(torch.int16))
+    cairn_b200.stream_status()
+    with pytest.raises(cairn_b200.CairnError):  # a B of the wrong shape, resident or not
+        hg.submit(_host(cases[0][0], (m, k)), b_dev[:-1], resident, bias_dev)
+
+
 def test_bias_relu_bf16_from_host(cuda):
     m, n, k = 512, 1024, 256
     a, b, bias = _case(m, n, k, 7)

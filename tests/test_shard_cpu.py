@@ -1,7 +1,8 @@
 """The multi-GPU host logic at world size 2 on CPU (gloo): the range and row-block partitions, the exact combination
 of ranks' f32 sum parts through an all-gather and the library's host combine, and the rank-order fold of u64 parts
 with its overflow rule. Each rank's part is formed here exactly from its terms (the device forms it on a GPU); the
-combined total must equal the oracle's exact sum of all terms, bit for bit."""
+combined total must equal the oracle's exact sum of all terms, bit for bit. The row all-gather (gather_rows) of
+even and uneven row blocks gives every rank the whole matrix."""
 
 from __future__ import annotations
 
@@ -96,3 +97,33 @@ def test_an_empty_rank_keeps_the_sign_of_an_all_negative_zero_sum():
     assert np.float32(shard.combine_f32_parts(parts)).view(np.uint32) == 0
     parts = torch.tensor([[1.0, 0.0, 24.0], [float("inf"), 0.0, 26.0]], dtype=torch.float64)
     assert shard.combine_f32_parts(parts) == float("inf")
+
+
+def _gather_worker(rank: int, world: int, port: int, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        got = []
+        for m in (12, 13, 2):  # equal blocks, then blocks of 5, 4, 4 rows, then an empty block
+            whole = torch.arange(m * 5, dtype=torch.float32).view(m, 5) * 1.5 - 7
+            lo, hi = shard.row_block(m, world, rank)
+            got.append(bool(torch.equal(shard.gather_rows(whole[lo:hi].clone(), m), whole)))
+        q.put((rank, got))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_row_blocks_gather_into_the_whole_matrix_on_every_rank():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 28500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_gather_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.terminate()
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert results == {r: [True, True, True] for r in range(3)}
