@@ -26,7 +26,10 @@
 #include <cstdint>
 #include <cstdlib>
 #include <cstring>
+#include <mutex>
 #include <type_traits>
+#include <utility>
+#include <vector>
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
@@ -721,36 +724,72 @@ __device__ __forceinline__ std::size_t partial_cell(int w, int ci, int chunks) {
   return static_cast<std::size_t>(w * chunks + ci) * 256;
 }
 
+// One output tile of the pair kernel: rows [256 mb, 256 mb + 256) and `units` blocks of 128 columns from column n0.
+struct TileSpec {
+  int mb, n0, units;
+};
+
+// A planned cover of the output (mixed tile widths; the host's planner, pair_tiles_plan): each pair's tiles listed in
+// turn, packed as band << 16 | first 128-column unit << 3 | units. Unplanned launches cover the output uniformly with
+// tiles of G * 256 columns in the order tile_of gives.
+constexpr int PLAN_MAX_PAIRS = 128, PLAN_MAX_TILES = 512;
+struct PairTiles {
+  int planned;
+  std::uint16_t first[PLAN_MAX_PAIRS + 1];  // pair q's tiles are tile[first[q]] .. tile[first[q + 1] - 1]
+  std::uint32_t tile[PLAN_MAX_TILES];
+};
+
 struct PairWork {
   long long u, u_end;  // stream-K: this pair's units
-  int t, tiles, pairs, num_kb;
+  int t, tiles, pairs, num_kb, num_m, num_n, tile_n;
   bool sk;
-  __device__ PairWork(int pair, int pairs_, int tiles_, int num_kb_, bool streamk)
-      : t(pair), tiles(tiles_), pairs(pairs_), num_kb(num_kb_), sk(streamk) {
-    const long long units = static_cast<long long>(tiles_) * num_kb_;
+  const PairTiles* plan;
+  int q, q_end;  // planned: this pair's entries of the table
+  __device__ PairWork(int pair, int pairs_, int num_m_, int num_n_, int tile_n_, int num_kb_, bool streamk,
+                      const PairTiles* plan_)
+      : t(pair), tiles(num_m_ * num_n_), pairs(pairs_), num_kb(num_kb_), num_m(num_m_), num_n(num_n_),
+        tile_n(tile_n_), sk(streamk), plan(plan_), q(0), q_end(0) {
+    const long long units = static_cast<long long>(tiles) * num_kb_;
     u = units * pair / pairs_;
     u_end = units * (pair + 1) / pairs_;
+    if (plan->planned) {
+      q = plan->first[pair];
+      q_end = plan->first[pair + 1];
+    }
   }
-  __device__ bool next(int& tile, int& kb0, int& kb1) {
+  __device__ bool next(TileSpec& ts, int& kb0, int& kb1) {
+    int tile;
+    if (plan->planned) {
+      if (q >= q_end) return false;
+      const std::uint32_t e = plan->tile[q++];
+      ts = {static_cast<int>(e >> 16), static_cast<int>((e >> 3) & 0x1fffu) * 128, static_cast<int>(e & 7u)};
+      kb0 = 0;
+      kb1 = num_kb;
+      return true;
+    }
     if (!sk) {
       if (t >= tiles) return false;
       tile = t;
       kb0 = 0;
       kb1 = num_kb;
       t += pairs;
-      return true;
+    } else {
+      if (u >= u_end) return false;
+      tile = static_cast<int>(u / num_kb);
+      kb0 = static_cast<int>(u % num_kb);
+      const long long left = u_end - u;
+      kb1 = left < num_kb - kb0 ? kb0 + static_cast<int>(left) : num_kb;
+      u += kb1 - kb0;
     }
-    if (u >= u_end) return false;
-    tile = static_cast<int>(u / num_kb);
-    kb0 = static_cast<int>(u % num_kb);
-    const long long left = u_end - u;
-    kb1 = left < num_kb - kb0 ? kb0 + static_cast<int>(left) : num_kb;
-    u += kb1 - kb0;
+    int nb;
+    tile_of(tile, num_m, num_n, ts.mb, nb);
+    ts.n0 = nb * tile_n;
+    ts.units = tile_n / 128;
     return true;
   }
   // The first unit of pair q's range.
-  __device__ long long start_of(int q) const {
-    return static_cast<long long>(tiles) * num_kb * q / pairs;
+  __device__ long long start_of(int qq) const {
+    return static_cast<long long>(tiles) * num_kb * qq / pairs;
   }
 };
 
@@ -790,7 +829,7 @@ template <int FMT, int G, int EPI>
 __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
     tc_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
                         const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_m,
-                        const TcParams p) {
+                        const TcParams p, const __grid_constant__ PairTiles plan) {
   using F = Fmt<FMT>;
   using S = PairShape<G>;
   constexpr bool READS = EPI == 1;
@@ -801,7 +840,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
   constexpr int MMA_K_ROWS = MMA_K_BYTES / F::bytes;
   constexpr int HALF = PAIR_BN / 2;               // rows of A, and columns of B per group, each CTA stages
   constexpr int GROUP_BYTES = HALF * SLICE;       // one column group's half in a stage
-  constexpr int COLS_PER_WARP = S::TILE_N / 2;    // each of the two warps on a lane quarter drains half the columns
+  constexpr int UNIT_BYTES = (HALF / 2) * SLICE;  // a CTA's share of one 128-column unit of B in a stage
 
   extern __shared__ std::uint8_t smem_raw[];
   std::uint8_t* base = reinterpret_cast<std::uint8_t*>((reinterpret_cast<std::uintptr_t>(smem_raw) + 1023) &
@@ -867,17 +906,18 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
   if (warp == 0) {
     if (lane == 0) {
       std::uint32_t stage = 0, phase = 0;
-      PairWork work(pair, pairs, tiles, num_kb, p.streamk != 0);
-      int t, kb_begin, kb_end;
-      while (work.next(t, kb_begin, kb_end)) {
-        int mb, nb;
-        tile_of(t, num_m, num_n, mb, nb);
-        const int m0 = mb * 2 * HALF + static_cast<int>(rank) * HALF;  // this CTA's rows of A
-        const int n_tile = nb * S::TILE_N;
+      PairWork work(pair, pairs, num_m, num_n, S::TILE_N, num_kb, p.streamk != 0, &plan);
+      TileSpec ts;
+      int kb_begin, kb_end;
+      while (work.next(ts, kb_begin, kb_end)) {
+        const int m0 = ts.mb * 2 * HALF + static_cast<int>(rank) * HALF;  // this CTA's rows of A
+        const int n_tile = ts.n0;
+        const int u0 = ts.units < 2 ? ts.units : 2, u1 = ts.units - u0;  // units of the two column groups
+        const std::uint32_t stage_bytes = 2u * (A_STAGE + static_cast<std::uint32_t>(ts.units) * UNIT_BYTES);
         for (int kb = kb_begin; kb < kb_end; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, abort_flag, p.fault, FAULT_WAIT_EMPTY)) goto producer_done;
           const std::uint32_t leader_full = cluster_addr(&full[stage], 0);
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2u * (A_STAGE + S::B_HALF));
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], stage_bytes);
           const std::uint32_t a_dst = smem_u32(a_smem + stage * A_STAGE);
           const std::uint32_t b_dst = smem_u32(b_smem + stage * S::B_HALF);
           const int k0 = kb * CH;
@@ -890,13 +930,15 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
           }
 #pragma unroll
           for (int g = 0; g < G; ++g) {
-            const int n0 = n_tile + g * PAIR_BN + static_cast<int>(rank) * HALF;  // this CTA's columns of group g
+            const int ug = g == 0 ? u0 : u1;
+            if (ug == 0) continue;
+            // this CTA's columns of group g: the group's first or second half (64 ug columns each)
+            const int n0 = n_tile + g * PAIR_BN + static_cast<int>(rank) * (HALF / 2) * ug;
             const std::uint32_t dst = b_dst + g * GROUP_BYTES;
-            if (p.b_k) {
+            if (p.b_k) {  // K-major B: one box of a whole group's half (uniform tiles only)
               tma_load_2d_pair(dst, &tm_b, leader_full, k0, n0);
             } else {
-#pragma unroll
-              for (int c = 0; c < HALF / CH; ++c)
+              for (int c = 0; c < (HALF / 2) * ug / CH; ++c)
                 tma_load_2d_pair(dst + c * CH * SLICE, &tm_b, leader_full, n0 + c * CH, k0);
             }
           }
@@ -911,8 +953,10 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0 && rank == 0) {
-      const std::uint32_t idesc =
+      const std::uint32_t idesc_full =
           idesc_make(F::code, F::code, p.a_mn != 0, p.b_k == 0, static_cast<std::uint32_t>(2 * HALF), PAIR_BN);
+      const std::uint32_t idesc_half =
+          idesc_make(F::code, F::code, p.a_mn != 0, p.b_k == 0, static_cast<std::uint32_t>(2 * HALF), PAIR_BN / 2);
       constexpr bool MN32 = F::bytes == 4;
       const std::uint32_t a_layout = (MN32 && p.a_mn) ? LAYOUT_SW128_32B : LAYOUT_SW128;
       const std::uint32_t b_layout = (MN32 && !p.b_k) ? LAYOUT_SW128_32B : LAYOUT_SW128;
@@ -920,9 +964,12 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       const std::uint32_t b_sbo = b_layout == LAYOUT_SW128_32B ? 512u : 1024u;
       const std::uint32_t a_lbo = p.a_mn ? CH * SLICE : 16u, b_lbo = p.b_k ? 16u : CH * SLICE;
       std::uint32_t stage = 0, phase = 0, it = 0;
-      PairWork work(pair, pairs, tiles, num_kb, p.streamk != 0);
-      int t, kb_begin, kb_end;
-      for (; work.next(t, kb_begin, kb_end); ++it) {
+      PairWork work(pair, pairs, num_m, num_n, S::TILE_N, num_kb, p.streamk != 0, &plan);
+      TileSpec ts;
+      int kb_begin, kb_end;
+      for (; work.next(ts, kb_begin, kb_end); ++it) {
+        const int u0 = ts.units < 2 ? ts.units : 2, u1 = ts.units - u0;
+        const std::uint32_t idesc0 = u0 == 2 ? idesc_full : idesc_half, idesc1 = u1 == 2 ? idesc_full : idesc_half;
         const std::uint32_t acc = S::ACCS == 2 ? (it & 1u) : 0u;
         const std::uint32_t acc_phase = S::ACCS == 2 ? ((it >> 1) & 1u) : (it & 1u);
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, abort_flag, p.fault, FAULT_WAIT_TEMPTY)) goto mma_done;
@@ -938,11 +985,11 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
             const std::uint32_t a_off = p.a_mn ? kk * (MMA_K_ROWS / 8) * 1024 : kk * MMA_K_BYTES;
             const std::uint32_t b_off = p.b_k ? kk * MMA_K_BYTES : kk * (MMA_K_ROWS / 8) * 1024;
             const std::uint64_t a_desc = sdesc(a_addr + a_off, a_lbo, a_sbo, a_layout);
-#pragma unroll
-            for (int g = 0; g < G; ++g)
-              umma_pair<F::kind>(d_tmem + g * PAIR_BN, a_desc,
-                                 sdesc(b_addr + g * GROUP_BYTES + b_off, b_lbo, b_sbo, b_layout), idesc,
-                                 (kb != kb_begin || kk != 0) ? 1u : 0u);
+            const std::uint32_t accumulate = (kb != kb_begin || kk != 0) ? 1u : 0u;
+            umma_pair<F::kind>(d_tmem, a_desc, sdesc(b_addr + b_off, b_lbo, b_sbo, b_layout), idesc0, accumulate);
+            if (G == 2 && u1 != 0)
+              umma_pair<F::kind>(d_tmem + PAIR_BN, a_desc, sdesc(b_addr + GROUP_BYTES + b_off, b_lbo, b_sbo, b_layout),
+                                 idesc1, accumulate);
           }
           tc_commit_pair(cluster_addr(&empty[stage], 0));
           tc_commit_pair(cluster_addr(&empty[stage], 1));
@@ -962,27 +1009,28 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
   } else {
     const int quarter = warp & 3;                       // TMEM lanes 32 * (warp id % 4) .. + 31
     const int ew = warp - 2;                            // epilogue warp 0..EPI_WARPS-1
-    const int col0 = (ew / 4) * COLS_PER_WARP;          // this warp's half of the tile's columns
-    constexpr int CHUNKS = COLS_PER_WARP / 32;
+    constexpr int CHUNKS = S::TILE_N / 64;              // chunks per warp of a uniform tile (the stream-K slots)
     constexpr std::size_t SLOT = static_cast<std::size_t>(S::EPI_WARPS) * CHUNKS * 32 * 32;  // floats per slot
     std::uint8_t* stage = epi_stage + ew * STAGE_BYTES;
     MaskTiles mt{&tm_m, &mask_bars[ew], 0u, abort_flag};
     std::uint32_t it = 0;
-    PairWork work(pair, pairs, tiles, num_kb, p.streamk != 0);
-    int t, kb_begin, kb_end;
-    for (; work.next(t, kb_begin, kb_end); ++it) {
+    PairWork work(pair, pairs, num_m, num_n, S::TILE_N, num_kb, p.streamk != 0, &plan);
+    TileSpec ts;
+    int kb_begin, kb_end;
+    for (; work.next(ts, kb_begin, kb_end); ++it) {
       const std::uint32_t acc = S::ACCS == 2 ? (it & 1u) : 0u;
       const std::uint32_t acc_phase = S::ACCS == 2 ? ((it >> 1) & 1u) : (it & 1u);
-      int mb, nb;
-      tile_of(t, num_m, num_n, mb, nb);
-      const int row0 = mb * 2 * HALF + static_cast<int>(rank) * HALF + quarter * 32;
-      const int c_first = nb * S::TILE_N + col0;  // this warp's first output column of the tile
+      // each of the two warps on a lane quarter drains half the tile's columns, 32 at a time
+      const int cols_per_warp = ts.units * 64, chunks = ts.units * 2;
+      const int col0 = (ew / 4) * cols_per_warp;
+      const int row0 = ts.mb * 2 * HALF + static_cast<int>(rank) * HALF + quarter * 32;
+      const int c_first = ts.n0 + col0;  // this warp's first output column of the tile
       // The tile's bias for this warp's columns, staged in shared memory while the MMAs run: read from global
       // memory chunk by chunk during the drain, each chunk's bias waited on L2 (shared memory leaves L1 little room),
       // and the next tile's MMAs wait for the drain. (The drain of the tile before has finished with the buffer.)
       float* bias_s = p.bias != nullptr ? epi_bias + ew * (S::BIAS_BYTES / 4) : nullptr;
       if (bias_s != nullptr) {
-        for (int i = lane; i < COLS_PER_WARP; i += 32) {
+        for (int i = lane; i < cols_per_warp; i += 32) {
           const int c = c_first + i;
           bias_s[i] = c < p.n ? __ldg(p.bias + c) : 0.0f;
         }
@@ -990,9 +1038,9 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       }
       if constexpr (READS || MASKED) {
         if (p.mask != nullptr)
-          prefetch_row_span(p.mask, 2, p, row0 + lane, c_first, c_first + COLS_PER_WARP);
+          prefetch_row_span(p.mask, 2, p, row0 + lane, c_first, c_first + cols_per_warp);
         else if (p.out_kind == OUT_ACC_F32 && kb_begin == 0 && kb_end == num_kb)
-          prefetch_row_span(p.out, 4, p, row0 + lane, c_first, c_first + COLS_PER_WARP);
+          prefetch_row_span(p.out, 4, p, row0 + lane, c_first, c_first + cols_per_warp);
       }
       if (!mbar_wait(&tfull[acc], acc_phase, abort_flag, p.fault, FAULT_WAIT_TFULL)) break;
       tc_fence_after();
@@ -1010,7 +1058,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
             __stcg(dst + q * 32, make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
                                              __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3])));
         } else {
-          store_chunk_staged<READS, MASKED>(p, row0, nb * S::TILE_N + col0 + ci * 32, r, stage, lane,
+          store_chunk_staged<READS, MASKED>(p, row0, c_first + ci * 32, r, stage, lane,
                                     bias_s != nullptr ? bias_s + ci * 32 : nullptr, &tm_c, mt);
         }
       };
@@ -1018,11 +1066,11 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
         // An epilogue that reads memory (the ReLU-gradient mask, or the old outputs of the accumulate form) keeps
         // those loads in flight rather than the TMEM loads: single-buffered, so its registers hold a chunk's loads.
 #pragma unroll 1
-        for (int ci = 0; ci < CHUNKS; ++ci) {
+        for (int ci = 0; ci < chunks; ++ci) {
           std::uint32_t r[32];
           tmem_ld_32x32b_x32(t_row + col0 + ci * 32, r);
           tmem_wait_ld(r);
-          if (ci + 1 == CHUNKS) {  // this warp's part of the accumulator is in registers
+          if (ci + 1 == chunks) {  // this warp's part of the accumulator is in registers
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cluster(cluster_addr(&tempty[acc], 0));
@@ -1032,19 +1080,19 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
       } else {
         // Otherwise the drain is double-buffered: a TMEM load takes several hundred cycles to reach the registers,
         // so each chunk's load is issued before the chunk ahead of it is written out. The accumulator goes back to
-        // the MMA issuer once the last chunk's load has landed. CHUNKS is even (8 for G = 2, 4 for G = 1). Outputs
+        // the MMA issuer once the last chunk's load has landed. `chunks` is even (twice the tile's units). Outputs
         // that leave by plain TMA stores (bf16) or TMA stores and reduce-adds (f32) run the loop with their own
         // compact chunk bodies.
         auto drain_chunks = [&](auto&& put) {
           std::uint32_t ra[32], rb[32];
           tmem_ld_32x32b_x32(t_row + col0, ra);
 #pragma unroll 1
-          for (int ci = 0; ci < CHUNKS; ci += 2) {
+          for (int ci = 0; ci < chunks; ci += 2) {
             tmem_wait_ld(ra);
             tmem_ld_32x32b_x32(t_row + col0 + (ci + 1) * 32, rb);
             put(ci, ra);
             tmem_wait_ld(rb);
-            if (ci + 2 < CHUNKS) {
+            if (ci + 2 < chunks) {
               tmem_ld_32x32b_x32(t_row + col0 + (ci + 2) * 32, ra);
             } else {  // this warp's part of the accumulator is in registers
               tc_fence_before();
@@ -1133,7 +1181,7 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
         tile_of(tt, num_m, num_n, mb, nb);
         const int w_quarter = (w + 2) & 3;  // epilogue warp w is warp w + 2: its TMEM lane quarter
         store_chunk_staged<READS, MASKED>(p, mb * 2 * HALF + rr * HALF + w_quarter * 32,
-                                  nb * S::TILE_N + (w / 4) * COLS_PER_WARP + ci * 32, r, stage, lane, nullptr,
+                                  nb * S::TILE_N + (w / 4) * (S::TILE_N / 2) + ci * 32, r, stage, lane, nullptr,
                                   &tm_c, mt);
       }
     }
@@ -1355,6 +1403,121 @@ PairPlan pair_plan(int tiles, int num_kb, int resident, int sms) {
   return PairPlan{static_cast<int>(pairs), true};
 }
 
+// ---- mixed-width tiles --------------------------------------------------------------------------------------------
+// The uniform cover (tiles of 256 x 512) leaves pairs idle in the last wave whenever the tile count is not near a
+// multiple of the pairs: 4096^3 has 128 tiles for 74 pairs, a second wave of 54 tiles in which 20 pairs wait, so the
+// product takes two tile-times for 1.73 tile-times of work. The planner covers each 256-row band with tiles of four
+// and three 128-column units (512 and 384 columns: every band of at least six units splits so), choosing per band how
+// many of each so that, dealt largest first to the least loaded pair, the most loaded pair holds as few units as
+// possible: for 4096^3, 74 tiles of 512 and 72 of 384 columns, seven units on every pair but two, where the uniform
+// cover puts eight on 54 of them. Tile widths are whole 64-column TMA boxes of B per CTA, so the plan is for 16-bit
+// operands with B row-major (the MN-major boxes); other shapes and formats keep the uniform cover. Kept per shape.
+struct PlannedShape {
+  std::uint64_t m, n;
+  int pairs;
+  bool ok;
+  PairTiles tiles;
+};
+
+// Units of the most loaded pair when tiles of 4 units (`fours`) and 3 units (`threes`) are dealt largest first to
+// the least loaded of `pairs` pairs.
+int lpt_makespan(long long fours, long long threes, int pairs) {
+  std::vector<int> load(static_cast<std::size_t>(pairs), 0);
+  auto deal = [&](long long count, int size) {
+    for (long long i = 0; i < count; ++i) {
+      std::size_t best = 0;
+      for (std::size_t q = 1; q < load.size(); ++q)
+        if (load[q] < load[best]) best = q;
+      load[best] += size;
+    }
+  };
+  deal(fours, 4);
+  deal(threes, 3);
+  int most = 0;
+  for (int v : load) most = v > most ? v : most;
+  return most;
+}
+
+bool plan_pair_tiles(const GemmArgs& g, int pairs, PairTiles* out) {
+  if ((g.fmt != FMT_BF16 && g.fmt != FMT_F16) || g.trans_b || pairs < 2 || pairs > PLAN_MAX_PAIRS) return false;
+  const long long num_m = static_cast<long long>((g.m + 255) / 256), units = static_cast<long long>((g.n + 127) / 128);
+  if (units < 6 || units > 8191 || num_m > 65535) return false;
+  const long long uniform_tiles = num_m * ((units + 3) / 4);
+  if (uniform_tiles < pairs || uniform_tiles > PLAN_MAX_TILES) return false;
+  const long long uniform = (uniform_tiles + pairs - 1) / pairs * 4;  // units on the most loaded pair
+  std::vector<std::pair<long long, long long>> ways;                // (fours, threes) covering one band
+  for (long long a = units / 4; a >= 0; --a)
+    if ((units - 4 * a) % 3 == 0) ways.push_back({a, (units - 4 * a) / 3});
+  long long best = uniform, best_tiles = 0, best_x = 0;
+  std::size_t best_i = 0, best_j = 0;
+  for (std::size_t i = 0; i < ways.size(); ++i)
+    for (std::size_t j = i; j < ways.size(); ++j)
+      for (long long x = 0; x <= num_m; ++x) {  // x bands split the first way, the rest the second
+        const long long fours = x * ways[i].first + (num_m - x) * ways[j].first;
+        const long long threes = x * ways[i].second + (num_m - x) * ways[j].second;
+        if (fours + threes > PLAN_MAX_TILES) continue;
+        const long long span = lpt_makespan(fours, threes, pairs);
+        if (span < best || (span == best && best_tiles && fours + threes < best_tiles)) {
+          best = span, best_tiles = fours + threes, best_i = i, best_j = j, best_x = x;
+        }
+        if (i == j) break;  // one way for every band: x does not matter
+      }
+  if (!best_tiles || best * 20 > uniform * 19) return false;  // keep the uniform cover unless 5 % or more is saved
+  // Lay the tiles out band by band (the band's four-unit tiles, then its three-unit ones), then deal them as above:
+  // all four-unit tiles in band order, then all three-unit ones, each to the least loaded pair.
+  std::vector<std::uint32_t> fours_list, threes_list;
+  for (long long band = 0; band < num_m; ++band) {
+    const auto& w = band < best_x ? ways[best_i] : ways[best_j];
+    long long unit = 0;
+    for (long long a = 0; a < w.first; ++a, unit += 4)
+      fours_list.push_back(static_cast<std::uint32_t>(band << 16 | unit << 3 | 4));
+    for (long long b = 0; b < w.second; ++b, unit += 3)
+      threes_list.push_back(static_cast<std::uint32_t>(band << 16 | unit << 3 | 3));
+  }
+  std::vector<int> load(static_cast<std::size_t>(pairs), 0);
+  std::vector<std::vector<std::uint32_t>> mine(static_cast<std::size_t>(pairs));
+  for (const auto* list : {&fours_list, &threes_list})
+    for (std::uint32_t e : *list) {
+      std::size_t q = 0;
+      for (std::size_t r = 1; r < load.size(); ++r)
+        if (load[r] < load[q]) q = r;
+      load[q] += static_cast<int>(e & 7u);
+      mine[q].push_back(e);
+    }
+  std::memset(out, 0, sizeof(*out));
+  out->planned = 1;
+  int k = 0;
+  for (int q = 0; q < pairs; ++q) {
+    out->first[q] = static_cast<std::uint16_t>(k);
+    for (std::uint32_t e : mine[static_cast<std::size_t>(q)]) out->tile[k++] = e;
+  }
+  out->first[pairs] = static_cast<std::uint16_t>(k);
+  return true;
+}
+
+// The plan for (g, pairs), made once per shape: false when the uniform cover stands. CAIRN_B200_PLAN=0 keeps the
+// uniform cover (for measuring the two against each other).
+bool pair_tiles_plan(const GemmArgs& g, int pairs, PairTiles* out) {
+  static const bool on = [] {
+    const char* v = std::getenv("CAIRN_B200_PLAN");
+    return !(v && v[0] == '0');
+  }();
+  if (!on || (g.fmt != FMT_BF16 && g.fmt != FMT_F16) || g.trans_b) return false;
+  static std::mutex mu;
+  static std::vector<PlannedShape> cache;
+  std::lock_guard<std::mutex> hold(mu);
+  for (const auto& c : cache)
+    if (c.m == g.m && c.n == g.n && c.pairs == pairs) {
+      if (c.ok) *out = c.tiles;
+      return c.ok;
+    }
+  PlannedShape made{g.m, g.n, pairs, false, {}};
+  made.ok = plan_pair_tiles(g, pairs, &made.tiles);
+  if (cache.size() < 64) cache.push_back(made);
+  if (made.ok) *out = made.tiles;
+  return made.ok;
+}
+
 template <int FMT, int BN>
 cudaError_t launch_tc(const GemmArgs& g, const TcParams& p, cudaStream_t stream, int sms) {
   using S = Shape<BN>;
@@ -1469,7 +1632,14 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   const int num_kb = (p.k + CH - 1) / CH;
   PairPlan plan = pair_plan(tiles, num_kb, resident_pairs<G>(sms), sms);
   if (plan.streamk && g.ws == nullptr) plan = pair_plan(tiles, num_kb, 0, sms);  // no workspace: data-parallel
-  const int pairs = plan.pairs;
+  int pairs = plan.pairs;
+  // Mixed-width tiles where the uniform cover's last wave leaves pairs idle (data-parallel G = 2 launches only).
+  static thread_local PairTiles cover;
+  cover.planned = 0;
+  if (G == 2 && !plan.streamk) {
+    const int resident = resident_pairs<G>(sms);
+    if (resident > 0 && pair_tiles_plan(g, resident, &cover)) pairs = resident;
+  }
   TcParams q = p;
   q.streamk = plan.streamk;
   q.flags = static_cast<std::uint32_t*>(g.ws);  // the workspace: the barrier's arrival counter, then the slots
@@ -1496,9 +1666,9 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = pdl_on ? 2 : 1;
-  e = epi == 2   ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 2>, ta, tb, tc, tm, q)
-      : epi == 1 ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 1>, ta, tb, tc, tm, q)
-                 : cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 0>, ta, tb, tc, tm, q);
+  e = epi == 2   ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 2>, ta, tb, tc, tm, q, cover)
+      : epi == 1 ? cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 1>, ta, tb, tc, tm, q, cover)
+                 : cudaLaunchKernelEx(&cfg, tc_gemm_pair_kernel<FMT, G, 0>, ta, tb, tc, tm, q, cover);
   if (e != cudaSuccess) return e;
   return cudaGetLastError();
 }

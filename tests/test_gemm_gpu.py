@@ -165,6 +165,98 @@ def test_fused_bias_relu_bf16_epilogue(cuda, relu, shape):
         assert (inputs.decode("bf16", got_bits) >= 0).all()
 
 
+# ---- mixed-width tiles: shapes whose uniform 256 x 512 cover leaves pairs idle get tiles of 512 and 384 columns ----
+PLANNED = [(2900, 3900, 72), (3072, 4096, 64), (2816, 3200, 136)]
+
+
+@pytest.mark.parametrize("shape", PLANNED)
+def test_planned_tiles_bias_relu_bf16_against_the_oracle(cuda, shape):
+    """Shapes the host's tile planner covers with 512- and 384-column tiles (ragged bands and a ragged last unit in
+    the first): bf16(relu(acc + bias)) within one bf16 rounding of the oracle's epilogue, every element."""
+    m, n, k = shape
+    rng = np.random.default_rng(m)
+    a = inputs.encode("bf16", rng.standard_normal(m * k))
+    b = inputs.encode("bf16", rng.standard_normal(k * n))
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    acc = restated.mma("bf16", np.zeros(m * n, np.float32), a, b, m, n, k)
+    want = restated.bias_act(acc, bias, True, m, n)
+    at, bt = to_dev("bf16", a, cuda).view(m, k), to_dev("bf16", b, cuda).view(k, n)
+    got = cairn_b200.gemm(at, bt, bias=torch.from_numpy(bias).to(cuda), relu=True, out_dtype=torch.bfloat16)
+    cairn_b200.stream_status()
+    got_bits = got.view(torch.int16).cpu().numpy().view(np.uint16).ravel()
+    assert _bf16_close(got_bits, want, 2 * bound("bf16", np.zeros(m * n, np.float32), a, b, m, n, k)).all()
+
+
+@pytest.mark.parametrize("fmt", ["bf16", "f16"])
+@pytest.mark.parametrize("form", ["accumulate", "store", "transposed_a"])
+def test_planned_tiles_f32_outputs_against_the_oracle(cuda, fmt, form):
+    """The planned cover with the f32 epilogues: mma_unordered's C += A B (TMA reduce-adds), C = A B stored, and A
+    read transposed (the planner keeps the tiles; A's layout does not enter them)."""
+    m, n, k = 2900, 3900, 72
+    c, a, b = inputs.mma_case(fmt, m, n, k, seed=k)
+    if form == "accumulate":
+        want = restated.mma(fmt, c, a, b, m, n, k)
+        ct = torch.from_numpy(c.copy()).to(cuda)
+        cairn_b200.mma_unordered(m, n, k, ct, to_dev(fmt, a, cuda), to_dev(fmt, b, cuda))
+        tol = 2 * bound(fmt, c, a, b, m, n, k)
+    else:
+        want = restated.mma(fmt, np.zeros(m * n, np.float32), a, b, m, n, k)
+        a_dev = to_dev(fmt, a, cuda).view(m, k)
+        if form == "transposed_a":
+            a_dev = a_dev.t().contiguous()
+        ct = cairn_b200.gemm(a_dev, to_dev(fmt, b, cuda).view(k, n), trans_a=form == "transposed_a",
+                             out_dtype=torch.float32)
+        tol = 2 * bound(fmt, np.zeros(m * n, np.float32), a, b, m, n, k)
+    cairn_b200.stream_status()
+    assert within(ct.cpu().numpy().ravel(), want.ravel(), tol).all()
+
+
+_UNIFORM_COVER = r"""
+import sys
+sys.path[:0] = [sys.argv[1], sys.argv[1] + "/tests"]
+import numpy as np, torch
+import cairn_b200
+d = dict(np.load(sys.argv[2]))
+dev = torch.device("cuda", 0)
+m, n, k = (int(v) for v in d["mnk"])
+a = torch.from_numpy(d["a"].view(np.int16)).to(dev).view(torch.bfloat16).view(m, k)
+b = torch.from_numpy(d["b"].view(np.int16)).to(dev).view(torch.bfloat16).view(k, n)
+out = cairn_b200.gemm(a, b, bias=torch.from_numpy(d["bias"]).to(dev), relu=True, out_dtype=torch.bfloat16)
+f32 = cairn_b200.gemm(a, b, out_dtype=torch.float32)
+cairn_b200.stream_status()
+np.savez(sys.argv[3], bf16=out.view(torch.int16).cpu().numpy(), f32=f32.cpu().numpy())
+"""
+
+
+@pytest.mark.parametrize("shape", [(4096, 4096, 256), (2900, 3900, 72)])
+def test_planned_and_uniform_covers_give_the_same_bits(cuda, tmp_path, shape):
+    """Each output's k order is the same whatever the width of the tile that holds it, so the planned cover and the
+    uniform one (CAIRN_B200_PLAN=0, in a child process) give the same bits: no tile is missed or run twice."""
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    m, n, k = shape
+    rng = np.random.default_rng(k)
+    a = inputs.encode("bf16", rng.standard_normal(m * k))
+    b = inputs.encode("bf16", rng.standard_normal(k * n))
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    src, dst = tmp_path / "in.npz", tmp_path / "out.npz"
+    np.savez(src, a=a, b=b, bias=bias, mnk=np.asarray(shape))
+    root = str(Path(__file__).resolve().parents[1])
+    done = subprocess.run([sys.executable, "-c", _UNIFORM_COVER, root, str(src), str(dst)], capture_output=True,
+                          text=True, timeout=600, env=dict(os.environ, CAIRN_B200_PLAN="0"))
+    assert done.returncode == 0, done.stderr[-3000:]
+    uniform = np.load(dst)
+    at, bt = to_dev("bf16", a, cuda).view(m, k), to_dev("bf16", b, cuda).view(k, n)
+    planned = cairn_b200.gemm(at, bt, bias=torch.from_numpy(bias).to(cuda), relu=True, out_dtype=torch.bfloat16)
+    planned_f32 = cairn_b200.gemm(at, bt, out_dtype=torch.float32)
+    cairn_b200.stream_status()
+    assert np.array_equal(planned.view(torch.int16).cpu().numpy(), uniform["bf16"])
+    assert np.array_equal(planned_f32.cpu().numpy().view(np.uint32), uniform["f32"].view(np.uint32))
+
+
 def test_tf32_multiply_of_f32_operands(cuda):
     m, n, k = 300, 264, 392
     rng = np.random.default_rng(12)
