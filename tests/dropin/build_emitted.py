@@ -16,6 +16,13 @@ For every program under tests/dropin/programs/ (CAIRN source):
 tests/dropin/scan_probe.cu, which exposes the B200 scan kernel alone (entries no CAIRN program emits), is built over
 the drop-in headers with the same device flags into tests/dropin/_build/libscanprobe.so.
 
+Kernel-benchmark submissions: each function of tests/dropin/harness/regions.cairn is exported with
+`cairn export --harness kernelbench --mapping kb_<name>.toml` by the reference compiler run from a copy of the
+reference's source tree whose runtime directory holds this project's drop-in region and collector headers
+(cairn_gpu.hpp, cairn_kernels.hpp, cairn_cub.hpp), so the submission (a KernelBench ModelNew that embeds the runtime
+headers it was exported with and builds them with torch's load_inline) runs the B200 machine. They land in
+tests/dropin/_build/harness/<name>/.
+
 The reference tree is named by the CAIRN_REFERENCE environment variable (the directory holding src/cairn), or by
 the first command-line argument. Nothing here is needed on a GPU box: the built libraries travel with the tree.
 
@@ -121,6 +128,36 @@ def build_probe(tree: Path) -> Path:
     return out
 
 
+HARNESS = HERE / "harness"
+HARNESS_OUT = BUILD / "harness"
+DROPIN_RUNTIME = ("cairn_gpu.hpp", "cairn_kernels.hpp", "cairn_cub.hpp")
+
+
+def build_harnesses(tree: Path) -> list[Path]:
+    """Every function of harness/regions.cairn exported as a KernelBench submission over the drop-in headers."""
+    done: list[Path] = []
+    with tempfile.TemporaryDirectory(prefix="cairn-overlay-") as tmp:
+        overlay = Path(tmp) / "src" / "cairn"
+        shutil.copytree(tree / "src" / "cairn", overlay, ignore=shutil.ignore_patterns("__pycache__"))
+        for name in DROPIN_RUNTIME:
+            shutil.copy2(DROPIN_HEADERS / name, overlay / "runtime" / name)
+        env = dict(os.environ, PYTHONPATH=str(Path(tmp) / "src"))
+        for mapping in sorted(HARNESS.glob("kb_*.toml")):
+            symbol = mapping.stem[3:]
+            out = HARNESS_OUT / symbol
+            if out.exists():
+                shutil.rmtree(out)
+            out.parent.mkdir(parents=True, exist_ok=True)
+            cmd = [sys.executable, "-m", "cairn", "export", str(HARNESS / "regions.cairn"), "--harness", "kernelbench",
+                   "--symbol", symbol, "--mapping", str(mapping), "--device-target", ARCH, "--cxx", "g++", "--out",
+                   str(out), "--format", "json"]
+            record = json.loads(_run(cmd, f"cairn export --harness of {symbol}", env=env, cwd=tmp, timeout=900).stdout)
+            if record.get("status") != "exported-harness":
+                raise RuntimeError(f"cairn export {symbol}: {record}")
+            done.append(out / record["file"])
+    return done
+
+
 def build(arg: str | None = None) -> list[Path]:
     """Builds every program both ways and the probe; returns the libraries written. Needs the reference tree."""
     tree = reference_tree(arg)
@@ -128,10 +165,11 @@ def build(arg: str | None = None) -> list[Path]:
         raise RuntimeError("the CAIRN reference tree is not available (set CAIRN_REFERENCE)")
     done: list[Path] = []
     with concurrent.futures.ThreadPoolExecutor(4) as pool:
-        jobs = [pool.submit(build_program, tree, p) for p in programs()] + [pool.submit(build_probe, tree)]
+        jobs = [pool.submit(build_program, tree, p) for p in programs()] + [pool.submit(build_probe, tree),
+                                                                             pool.submit(build_harnesses, tree)]
         for job in jobs:
             r = job.result()
-            done.extend(r if isinstance(r, tuple) else [r])
+            done.extend(r if isinstance(r, (tuple, list)) else [r])
     return done
 
 
