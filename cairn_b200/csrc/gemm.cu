@@ -799,11 +799,12 @@ struct PairWork {
 // rows [128 r, 128 r + 128) of the tile's A, and in each column group g the columns [256 g + 128 r, + 128) of B,
 // for pair rank r. The leader (rank 0) issues one pair MMA per column group and 32-byte k step; each MMA reads both
 // CTAs' halves and accumulates rows 128 r .. 128 r + 127, 256 columns, into rank r's tensor memory.
-//   Why two shapes: the operands reach the SMs from L2 at about 10 TB/s on a B200, and a 256 x 256 pair step
-//   (64 KB per 128-byte k slice per pair) saturates that near 1.3 PFLOP/s. A 256 x 512 tile (G = 2) reads A once for
-//   both column groups, 25 % fewer bytes per flop, at the price of a single accumulator (512 TMEM columns) whose
-//   drain the next tile waits for; G = 1 keeps two accumulators and hides the drain. Eight epilogue warps (two per
-//   TMEM lane quarter, each draining half the columns) keep that drain short.
+//   Why two shapes: a 256 x 256 pair step (G = 1) moves 64 KB per 128-byte k slice per pair, about 18 TB/s from L2
+//   at the tensor pipe's full rate, near the 20-24 TB/s a B200's L2 delivers to the SMs; it measured about 1.3
+//   PFLOP/s. A 256 x 512 tile (G = 2) reads A once for both column groups, 25 % fewer bytes per flop (about 13.7
+//   TB/s at full rate), at the price of a single accumulator (512 TMEM columns) whose drain the next tile waits for;
+//   G = 1 keeps two accumulators and hides the drain. Eight epilogue warps (two per TMEM lane quarter, each draining
+//   half the columns) keep that drain short.
 //   Both CTAs' TMA loads count their bytes on the leader's "full" barrier; the leader's commits arrive on the
 //   "empty" and "tmem full" barriers of both CTAs (one plain commit per CTA); every epilogue warp of the pair
 //   arrives on the leader's "tmem empty" barrier.
