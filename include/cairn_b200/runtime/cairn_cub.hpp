@@ -3,9 +3,9 @@
 // :7-36), and the older synchronous forms. Nothing here uses CUB (runtime/cairn_cub.hpp:14-25 calls DeviceReduce and
 // DeviceScan).
 //
-// B200::reduce: one launch of a device-sized persistent grid. Each thread loads eight values of a tile (four for
-// values wider than 8 bytes) before folding them into as many accumulators, so eight loads per thread are in flight;
-// the accumulators fold pairwise, each warp folds by shuffles, the block's eight warp totals fold in warp 0, one
+// B200::reduce: one launch of a device-sized persistent grid. Each thread loads eight values of a tile, so eight loads
+// per thread are in flight, before folding them in turn into its accumulators (eight for values of up to 4 bytes,
+// four for wider ones); the accumulators fold pairwise, each warp folds by shuffles, the block's eight warp totals fold in warp 0, one
 // partial per block goes to the scratch the context lends, and the last block to finish (an atomic ticket) folds
 // the partials and stores the total. The order of the folds is fixed by n and the device; the operator must be
 // associative and commutative, which every operator a device `reduce` admits is (+ over the checked Sum, add_wrap,
@@ -32,11 +32,18 @@ namespace b200 {
 
 constexpr unsigned FOLD_THREADS = 256;
 constexpr unsigned FOLD_WARPS = FOLD_THREADS / 32;
-constexpr unsigned FOLD_BLOCKS_PER_SM = 128;  // the grid: 128 blocks per SM at most (18,944 on a B200)
-// Independent accumulators per thread, which is also how many of a thread's loads are in flight at once: eight for
-// values of up to 4 bytes, four for wider ones. Measured on a B200 at n = 2^30: an f32 fold with 8 ran 7.2-7.4 TB/s
-// (4 or 16 no faster), a u64 fold over a 16-byte (value, flag) accumulator 7.4-7.5 with 4 and 7.0 with 8.
+// The grid: at most 128 blocks per SM (18,944 on a B200) for values of up to 8 bytes, 64 for wider ones, whose last
+// block's fold of the partials reads twice the bytes per block.
+template<class T> constexpr unsigned fold_blocks_per_sm() noexcept { return sizeof(T) <= 8 ? 128u : 64u; }
+// Independent accumulators per thread: eight for values of up to 4 bytes, four for wider ones. Measured on a B200 at
+// n = 2^30: an f32 fold with 8 ran 7.2-7.4 TB/s (4 or 16 no faster), a u64 fold over a 16-byte (value, flag)
+// accumulator 7.4-7.5 with 4 and 7.0 with 8.
 template<class T> constexpr unsigned fold_ways() noexcept { return sizeof(T) <= 4 ? 8u : 4u; }
+// A thread's loads in flight per round, folded into its accumulators in turn: eight whatever the width. Measured on a
+// B200 through the compiler-emitted checked u64 `reduce +` at n = 2^30 (16-byte accumulators): four loads a round
+// 7.02 TB/s, eight 7.10, sixteen 7.10, eight with 64 blocks per SM 7.14 (CUB on the same box: 7.19); the f32 fold
+// unchanged at 6.86-6.89.
+constexpr unsigned FOLD_LOADS = 8;
 
 inline std::size_t fold_partials_bytes(unsigned grid, std::size_t t_size) noexcept {
   return (std::size_t(grid) * t_size + 255) / 256 * 256;
@@ -92,32 +99,33 @@ template<class T, class Fold> __device__ inline T fold_block(T v, Fold& fold, T 
   return r;
 }
 
-// The reduction: a persistent grid over tiles of fold_ways<T>() * FOLD_THREADS consecutive values, each thread
-// loading its fold_ways values of a tile (coalesced: step k of a warp reads 32 consecutive values) before it folds
-// them into as many accumulators; the accumulators fold pairwise, the block folds by shuffles, one partial per block
+// The reduction: a persistent grid over tiles of L * FOLD_THREADS consecutive values, each thread loading its L values
+// of a tile (coalesced: step k of a warp reads 32 consecutive values) before it folds them into its K accumulators in
+// turn; the accumulators fold pairwise, the block folds by shuffles, one partial per block
 // lands in the scratch, and the last block to arrive (an atomic ticket) folds the partials and stores the total.
 // The order is fixed by n and the grid; every operator a device `reduce` admits is associative and commutative.
 template<class T, class In, class Out, class Fold>
 __global__ void __launch_bounds__(FOLD_THREADS)
     fold_kernel(In in, Out out, std::size_t n, Fold fold, T identity, T* partials, unsigned* ticket) {
   static_assert(alignof(T) <= 16, "a fold value fits the shared totals' alignment");
-  constexpr unsigned K = fold_ways<T>();
+  constexpr unsigned K = fold_ways<T>(), L = FOLD_LOADS > K ? FOLD_LOADS : K;
+  static_assert(L % K == 0, "each round's loads fold into the accumulators in turn");
   __shared__ __align__(16) unsigned char raw[FOLD_WARPS * sizeof(T)];
   __shared__ bool last;
   T* warp_totals = reinterpret_cast<T*>(raw);
   T acc[K];
 #pragma unroll
   for(unsigned k = 0; k < K; ++k) acc[k] = identity;
-  const std::size_t width = std::size_t(K) * FOLD_THREADS, whole = n / width;
+  const std::size_t width = std::size_t(L) * FOLD_THREADS, whole = n / width;
   std::size_t tile = blockIdx.x;
 #pragma unroll 1
   for(; tile < whole; tile += gridDim.x) {
     const std::size_t first = tile * width + threadIdx.x;
-    T v[K];
+    T v[L];
 #pragma unroll
-    for(unsigned k = 0; k < K; ++k) v[k] = in[first + std::size_t(k) * FOLD_THREADS];
+    for(unsigned k = 0; k < L; ++k) v[k] = in[first + std::size_t(k) * FOLD_THREADS];
 #pragma unroll
-    for(unsigned k = 0; k < K; ++k) acc[k] = fold(acc[k], v[k]);
+    for(unsigned k = 0; k < L; ++k) acc[k % K] = fold(acc[k % K], v[k]);
   }
   if(tile == whole)  // the partial tile, to the block the rotation hands it to
     for(std::size_t i = whole * width + threadIdx.x; i < n; i += FOLD_THREADS) acc[0] = fold(acc[0], in[i]);
@@ -158,12 +166,13 @@ __global__ void __launch_bounds__(FOLD_THREADS)
   }
 }
 
-// Blocks of one reduction: one per tile of n, at most FOLD_BLOCKS_PER_SM per SM. Measured on a B200 at n = 2^30
+// Blocks of one reduction: one per tile of n, at most fold_blocks_per_sm<T>() per SM. Measured on a B200 at n = 2^30
 // (f32, 8 accumulators): 18,944 blocks ran 7.23 TB/s, 65,535 7.41 and one resident wave (1,184) 6.27; the grid
 // stops at 18,944 so that the last block's fold of the partials stays a few microseconds.
 template<class T> inline unsigned fold_grid(std::size_t n) noexcept {
-  const std::size_t width = std::size_t(fold_ways<T>()) * FOLD_THREADS, needed = (n + width - 1) / width;
-  const std::size_t most = std::size_t(sm_count()) * FOLD_BLOCKS_PER_SM;
+  const std::size_t loads = FOLD_LOADS > fold_ways<T>() ? FOLD_LOADS : fold_ways<T>();
+  const std::size_t width = loads * FOLD_THREADS, needed = (n + width - 1) / width;
+  const std::size_t most = std::size_t(sm_count()) * fold_blocks_per_sm<T>();
   return unsigned(needed < most ? (needed ? needed : 1) : most);
 }
 
