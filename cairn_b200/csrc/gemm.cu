@@ -936,8 +936,9 @@ __global__ void __launch_bounds__(PairShape<G>::THREADS, 1)
             // this CTA's columns of group g: the group's first or second half (64 ug columns each)
             const int n0 = n_tile + g * PAIR_BN + static_cast<int>(rank) * (HALF / 2) * ug;
             const std::uint32_t dst = b_dst + g * GROUP_BYTES;
-            if (p.b_k) {  // K-major B: one box of a whole group's half (uniform tiles only)
-              tma_load_2d_pair(dst, &tm_b, leader_full, k0, n0);
+            if (p.b_k) {  // K-major B: one box of 64 rows (B's columns) per unit
+              for (int u = 0; u < ug; ++u)
+                tma_load_2d_pair(dst + u * UNIT_BYTES, &tm_b, leader_full, k0, n0 + u * (HALF / 2));
             } else {
               for (int c = 0; c < (HALF / 2) * ug / CH; ++c)
                 tma_load_2d_pair(dst + c * CH * SLICE, &tm_b, leader_full, n0 + c * CH, k0);
@@ -1411,8 +1412,9 @@ PairPlan pair_plan(int tiles, int num_kb, int resident, int sms) {
 // and three 128-column units (512 and 384 columns: every band of at least six units splits so), choosing per band how
 // many of each so that, dealt largest first to the least loaded pair, the most loaded pair holds as few units as
 // possible: for 4096^3, 74 tiles of 512 and 72 of 384 columns, seven units on every pair but two, where the uniform
-// cover puts eight on 54 of them. Tile widths are whole 64-column TMA boxes of B per CTA, so the plan is for 16-bit
-// operands with B row-major (the MN-major boxes); other shapes and formats keep the uniform cover. Kept per shape.
+// cover puts eight on 54 of them. Tile widths are whole 64-column TMA boxes of B per CTA (B row-major: boxes of 64
+// columns; B transposed: boxes of 64 of its rows), so the plan is for 16-bit operands in either layout; other shapes
+// and formats keep the uniform cover. Kept per shape.
 struct PlannedShape {
   std::uint64_t m, n;
   int pairs;
@@ -1440,7 +1442,7 @@ int lpt_makespan(long long fours, long long threes, int pairs) {
 }
 
 bool plan_pair_tiles(const GemmArgs& g, int pairs, PairTiles* out) {
-  if ((g.fmt != FMT_BF16 && g.fmt != FMT_F16) || g.trans_b || pairs < 2 || pairs > PLAN_MAX_PAIRS) return false;
+  if ((g.fmt != FMT_BF16 && g.fmt != FMT_F16) || pairs < 2 || pairs > PLAN_MAX_PAIRS) return false;
   const long long num_m = static_cast<long long>((g.m + 255) / 256), units = static_cast<long long>((g.n + 127) / 128);
   if (units < 6 || units > 8191 || num_m > 65535) return false;
   const long long uniform_tiles = num_m * ((units + 3) / 4);
@@ -1503,7 +1505,7 @@ bool pair_tiles_plan(const GemmArgs& g, int pairs, PairTiles* out) {
     const char* v = std::getenv("CAIRN_B200_PLAN");
     return !(v && v[0] == '0');
   }();
-  if (!on || (g.fmt != FMT_BF16 && g.fmt != FMT_F16) || g.trans_b) return false;
+  if (!on || (g.fmt != FMT_BF16 && g.fmt != FMT_F16)) return false;
   static std::mutex mu;
   static std::vector<PlannedShape> cache;
   std::lock_guard<std::mutex> hold(mu);
@@ -1604,7 +1606,9 @@ cudaError_t launch_pair(const GemmArgs& g, const TcParams& p, cudaStream_t strea
   CUtensorMap ta, tb;
   const bool ok_a = g.trans_a ? encode(&ta, FMT, g.a, g.m, g.k, es, CH, CH, true)
                               : encode(&ta, FMT, g.a, g.k, g.m, es, CH, HALF, false);
-  const bool ok_b = g.trans_b ? encode(&tb, FMT, g.b, g.k, g.n, es, CH, HALF, false)
+  // K-major B (stored n x k) comes in boxes of 64 of its rows, one per 128-column unit's half, so that tiles of any
+  // width take it.
+  const bool ok_b = g.trans_b ? encode(&tb, FMT, g.b, g.k, g.n, es, CH, HALF / 2, false)
                               : encode(&tb, FMT, g.b, g.n, g.k, es, CH, CH, true);
   if (!ok_a || !ok_b) return cudaErrorInvalidValue;
   // Outputs leave through TMA stores where the output's tensor map allows (bf16, f32 stored, f32 accumulated as a TMA

@@ -188,10 +188,11 @@ def test_planned_tiles_bias_relu_bf16_against_the_oracle(cuda, shape):
 
 
 @pytest.mark.parametrize("fmt", ["bf16", "f16"])
-@pytest.mark.parametrize("form", ["accumulate", "store", "transposed_a"])
+@pytest.mark.parametrize("form", ["accumulate", "store", "transposed_a", "transposed_b"])
 def test_planned_tiles_f32_outputs_against_the_oracle(cuda, fmt, form):
-    """The planned cover with the f32 epilogues: mma_unordered's C += A B (TMA reduce-adds), C = A B stored, and A
-    read transposed (the planner keeps the tiles; A's layout does not enter them)."""
+    """The planned cover with the f32 epilogues: mma_unordered's C += A B (TMA reduce-adds), C = A B stored, A read
+    transposed (A's layout does not enter the tiles), and B stored n x k (its K-major boxes of 64 rows, one per
+    128-column unit's half, take tiles of 3 units as well as 4)."""
     m, n, k = 2900, 3900, 72
     c, a, b = inputs.mma_case(fmt, m, n, k, seed=k)
     if form == "accumulate":
@@ -201,10 +202,12 @@ def test_planned_tiles_f32_outputs_against_the_oracle(cuda, fmt, form):
         tol = 2 * bound(fmt, c, a, b, m, n, k)
     else:
         want = restated.mma(fmt, np.zeros(m * n, np.float32), a, b, m, n, k)
-        a_dev = to_dev(fmt, a, cuda).view(m, k)
+        a_dev, b_dev = to_dev(fmt, a, cuda).view(m, k), to_dev(fmt, b, cuda).view(k, n)
         if form == "transposed_a":
             a_dev = a_dev.t().contiguous()
-        ct = cairn_b200.gemm(a_dev, to_dev(fmt, b, cuda).view(k, n), trans_a=form == "transposed_a",
+        if form == "transposed_b":
+            b_dev = b_dev.t().contiguous()
+        ct = cairn_b200.gemm(a_dev, b_dev, trans_a=form == "transposed_a", trans_b=form == "transposed_b",
                              out_dtype=torch.float32)
         tol = 2 * bound(fmt, np.zeros(m * n, np.float32), a, b, m, n, k)
     cairn_b200.stream_status()
@@ -223,8 +226,9 @@ a = torch.from_numpy(d["a"].view(np.int16)).to(dev).view(torch.bfloat16).view(m,
 b = torch.from_numpy(d["b"].view(np.int16)).to(dev).view(torch.bfloat16).view(k, n)
 out = cairn_b200.gemm(a, b, bias=torch.from_numpy(d["bias"]).to(dev), relu=True, out_dtype=torch.bfloat16)
 f32 = cairn_b200.gemm(a, b, out_dtype=torch.float32)
+tb = cairn_b200.gemm(a, b.t().contiguous(), trans_b=True, out_dtype=torch.float32)
 cairn_b200.stream_status()
-np.savez(sys.argv[3], bf16=out.view(torch.int16).cpu().numpy(), f32=f32.cpu().numpy())
+np.savez(sys.argv[3], bf16=out.view(torch.int16).cpu().numpy(), f32=f32.cpu().numpy(), tb=tb.cpu().numpy())
 """
 
 
@@ -252,9 +256,11 @@ def test_planned_and_uniform_covers_give_the_same_bits(cuda, tmp_path, shape):
     at, bt = to_dev("bf16", a, cuda).view(m, k), to_dev("bf16", b, cuda).view(k, n)
     planned = cairn_b200.gemm(at, bt, bias=torch.from_numpy(bias).to(cuda), relu=True, out_dtype=torch.bfloat16)
     planned_f32 = cairn_b200.gemm(at, bt, out_dtype=torch.float32)
+    planned_tb = cairn_b200.gemm(at, bt.t().contiguous(), trans_b=True, out_dtype=torch.float32)
     cairn_b200.stream_status()
     assert np.array_equal(planned.view(torch.int16).cpu().numpy(), uniform["bf16"])
     assert np.array_equal(planned_f32.cpu().numpy().view(np.uint32), uniform["f32"].view(np.uint32))
+    assert np.array_equal(planned_tb.cpu().numpy().view(np.uint32), uniform["tb"].view(np.uint32))
 
 
 def test_tf32_multiply_of_f32_operands(cuda):
