@@ -163,7 +163,30 @@ class ClockSampler:
         return out
 
 
-def time_steps(dist: Dist, stream, launch, steps: int, warmup: int):
+class DeviceClock:
+    """The SM clock inside a timed region, from the device itself: cairn_b200_clock_marks before and after the region
+    (every SM's %clock64 and %globaltimer), each SM's cycles over nanoseconds, the median over SMs. nvidia-smi samples
+    every 50 ms at best, longer than a 20-product region."""
+
+    SLOTS = 256
+
+    def __init__(self, dist: Dist):
+        import torch
+
+        self.lib = lib_handle()
+        self.marks = [torch.zeros(2 * self.SLOTS, dtype=torch.int64, device=dist.device) for _ in range(2)]
+
+    def mark(self, stream, which: int):
+        check(self.lib.cairn_b200_clock_marks(stream.cuda_stream, self.marks[which].data_ptr(), self.SLOTS),
+              "cairn_b200_clock_marks")
+
+    def mhz(self) -> float | None:
+        a, b = (m.view(-1, 2).cpu().tolist() for m in self.marks)
+        rates = [(c1 - c0) / (g1 - g0) * 1000 for (c0, g0), (c1, g1) in zip(a, b) if g0 and g1 > g0 and c1 > c0]
+        return statistics.median(rates) if rates else None
+
+
+def time_steps(dist: Dist, stream, launch, steps: int, warmup: int, clock: DeviceClock | None = None):
     """W warm-up steps, then K steps timed on `stream` with CUDA events (a barrier and a synchronize on both
     sides). Returns (max-over-ranks ms per step, this rank's ms per step, wall t0, wall t1).
 
@@ -182,10 +205,14 @@ def time_steps(dist: Dist, stream, launch, steps: int, warmup: int):
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     t0 = time.time()
+    if clock is not None:
+        clock.mark(stream, 0)
     start.record(stream)
     for i in range(steps):
         launch(warmup + i)
     end.record(stream)
+    if clock is not None:
+        clock.mark(stream, 1)
     torch.cuda.synchronize()
     t1 = time.time()
     dist.barrier()
@@ -865,9 +892,12 @@ def main() -> None:
     else:
         wl = Stream(dist, args.workload, args.log2n)
     peaks, peak_source = measured_peaks()
-    ms, launch_ms, t0, t1 = time_steps(dist, wl.stream, wl.launch, args.steps, args.warmup)
+    device_clock = DeviceClock(dist)
+    ms, launch_ms, t0, t1 = time_steps(dist, wl.stream, wl.launch, args.steps, args.warmup, device_clock)
     clocks = sampler.window(t0, t1)
     sampler.stop()
+    clocks["sm_mhz_in_region"] = device_clock.mhz()
+    clocks["in_region_note"] = "each SM's %clock64 cycles over %globaltimer ns across the timed region, median over SMs"
     if isinstance(wl, Scan):  # the roofline's kernel: the machine's scan alone, without the context's copy pass
         _, launch_ms, _, _ = time_steps(dist, wl.stream, wl.kernel_alone, args.steps, args.warmup)
     stat = lib_handle().cairn_b200_stream_status(wl.stream.cuda_stream)

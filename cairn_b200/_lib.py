@@ -50,6 +50,7 @@ SIGNATURES: dict[str, tuple] = {
     "cairn_b200_stream_status": (_i, [_p]),
     "cairn_b200_watchdog_selftest": (_i, [_p]),
     "cairn_b200_status_string": (C.c_char_p, [_i]),
+    "cairn_b200_clock_marks": (_i, [_p, _p, _z]),
     "cairn_b200_sm_count": (_i, []),
     "cairn_b200_version": (_i, []),
 }

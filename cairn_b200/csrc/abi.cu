@@ -495,6 +495,18 @@ const char* cairn_b200_status_string(int status) {
   }
 }
 
+int cairn_b200_clock_marks(void* stream, unsigned long long* slots, size_t count) {
+  int status;
+  const Device* d = current(&status);
+  if (!d) return status;
+  if (count == 0 || slots == nullptr || (reinterpret_cast<std::uintptr_t>(slots) & 7u) != 0) return CAIRN_B200_ERR_VIEW;
+  if (count > 0xffffffffu) return CAIRN_B200_ERR_ARG;
+  return clock_marks_launch(static_cast<cudaStream_t>(stream), slots, static_cast<unsigned>(count), d->sms) ==
+                 cudaSuccess
+             ? CAIRN_B200_OK
+             : CAIRN_B200_ERR_CUDA;
+}
+
 int cairn_b200_sm_count(void) {
   int status;
   const Device* d = current(&status);

@@ -54,6 +54,7 @@ cudaError_t sum_f32_launch(std::size_t n, const float* x, float* out_f32, double
                            cudaStream_t s, int sms);
 cudaError_t combine_f32_parts_launch(const double* parts, int count, float* out, cudaStream_t s);
 cudaError_t watchdog_launch(cudaStream_t s, std::uint32_t* fault);
+cudaError_t clock_marks_launch(cudaStream_t s, unsigned long long* slots, unsigned count, int sms);
 // out (bf16, n) = (y - t) * scale rounded to nearest-even, and the f64 sum of (y - t)^2 into `partials` (one
 // 32-byte cell per block, then the ticket); the last block writes loss[0] = f32(sum / n).
 cudaError_t mse_grad_launch(std::size_t n, const float* y, const float* t, std::uint16_t* dy, float scale,

@@ -532,6 +532,25 @@ __global__ void watchdog_kernel(std::uint32_t* fault) {
   if (threadIdx.x == 0) mbar_wait(&never, 0u, &abort_flag, fault, FAULT_WATCHDOG);
 }
 
+// Clock marks: each block's first thread writes its SM's cycle counter (%clock64) and the global nanosecond timer
+// into the SM's slot (%smid), so that two marks on a stream bracket the work between them: cycles over nanoseconds
+// per SM is that SM's average clock over the interval. Enough blocks that every SM holds at least one.
+__global__ void clock_marks_kernel(unsigned long long* slots, unsigned count) {
+  if (threadIdx.x != 0) return;
+  unsigned smid;
+  asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+  if (smid >= count) return;
+  long long cycles;
+  asm volatile("mov.u64 %0, %%clock64;" : "=l"(cycles));
+  slots[2 * smid] = static_cast<unsigned long long>(cycles);
+  slots[2 * smid + 1] = globaltimer();
+}
+
+cudaError_t clock_marks_launch(cudaStream_t s, unsigned long long* slots, unsigned count, int sms) {
+  clock_marks_kernel<<<4 * sms, 32, 0, s>>>(slots, count);
+  return cudaGetLastError();
+}
+
 cudaError_t watchdog_launch(cudaStream_t s, std::uint32_t* fault) {
   watchdog_kernel<<<1, 32, 0, s>>>(fault);
   return cudaGetLastError();

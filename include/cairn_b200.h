@@ -152,6 +152,12 @@ const char* cairn_b200_status_string(int status);
  * context stays usable), CAIRN_B200_ERR_DEVICE when no fault came back, or the failing status. No reference
  * counterpart: the reference's device guards trap and poison the context (runtime/cairn_kernels.hpp:33-59). */
 int cairn_b200_watchdog_selftest(void* stream);
+/* Clock marks, queued on `stream`: for each SM that runs one of the entry's blocks, slots[2 * smid] = its cycle
+ * counter (%clock64) and slots[2 * smid + 1] = the global nanosecond timer (%globaltimer), for smid < count (device
+ * memory, 2 * count 8-byte slots; SMs without a block keep what the slots held). Two marks bracket the work queued
+ * between them: an SM's cycles over nanoseconds is its average clock over that work. No reference counterpart: a
+ * measurement aid (bench.py reports the SM clock inside its timed region with it). */
+int cairn_b200_clock_marks(void* stream, unsigned long long* slots, size_t count);
 /* The number of SMs of the current device the kernels size their grids for, or a negative status. */
 int cairn_b200_sm_count(void);
 /* The ABI version: major * 10000 + minor * 100 + patch. */

@@ -50,3 +50,4 @@ def test_our_arm_line_on_config_2(cuda):
     assert e["h2d_bytes_per_step"] == 4096 * 4096 * 2 and e["d2h_bytes_per_step"] == 4096 * 4096 * 2
     assert d["gpu_launches"] == 3
     assert {"sm_mhz", "sm_max_mhz", "reasons"} <= d["clocks"].keys()
+    assert 300 < d["clocks"]["sm_mhz_in_region"] < 2100

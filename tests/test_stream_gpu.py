@@ -162,3 +162,29 @@ def test_mse_gradient_bit_for_bit_and_its_loss(cuda, n, offset):
     want_loss = np.float32(np.sum(d.astype(np.float64) ** 2) / n) if n else np.float32(0.0)
     got = np.float32(loss.item())
     assert abs(int(got.view(np.int32)) - int(want_loss.view(np.int32))) <= 1, (got, want_loss)
+
+
+def test_clock_marks_give_each_sms_clock_over_an_interval(cuda):
+    """cairn_b200_clock_marks before and after 50 ms of work on the stream: every SM wrote both marks (one block lands
+    on each SM at least), the timer advanced by the interval, and each SM's cycles over nanoseconds is a B200's clock
+    (between 0.3 and 2.1 GHz). A misaligned or null slot array is refused."""
+    from cairn_b200._lib import ERR_VIEW
+
+    lib = cairn_b200.lib()
+    stream = torch.cuda.current_stream(cuda)
+    sms = lib.cairn_b200_sm_count()
+    a = torch.zeros(512, dtype=torch.int64, device=cuda)
+    b = torch.zeros(512, dtype=torch.int64, device=cuda)
+    assert lib.cairn_b200_clock_marks(stream.cuda_stream, a.data_ptr(), 256) == 0
+    torch.cuda._sleep(100_000_000)  # about 50 ms of spinning on the stream
+    assert lib.cairn_b200_clock_marks(stream.cuda_stream, b.data_ptr(), 256) == 0
+    cairn_b200.stream_status()
+    a, b = a.view(-1, 2).cpu().numpy(), b.view(-1, 2).cpu().numpy()
+    seen = (a[:, 1] > 0) & (b[:, 1] > a[:, 1])
+    assert seen.sum() >= 0.9 * sms  # (%smid numbers the SMs; a block on each is all but certain)
+    ghz = (b[seen, 0] - a[seen, 0]) / (b[seen, 1] - a[seen, 1])
+    assert (ghz > 0.3).all() and (ghz < 2.1).all(), ghz
+    assert ((b[seen, 1] - a[seen, 1]) > 1_000_000).all()  # more than 1 ms between the marks
+    assert lib.cairn_b200_clock_marks(stream.cuda_stream, None, 256) == ERR_VIEW
+    c = torch.zeros(8, dtype=torch.int64, device=cuda)
+    assert lib.cairn_b200_clock_marks(stream.cuda_stream, c.data_ptr() + 4, 2) == ERR_VIEW
