@@ -474,3 +474,49 @@ def test_the_program_on_the_reference_machine_agrees_with_the_b200_machine(emitt
     tol = 2 * (k + 1) * 2.0**-22 * (np.abs(gc.reshape(m, n)) + av @ bv)
     assert (np.abs(ref["gemm"].reshape(m, n) - want_c) <= tol).all()
     assert (np.abs(ct.cpu().numpy().reshape(m, n) - want_c) <= tol).all()
+
+
+def test_emitted_entries_from_several_host_threads_at_once(emitted, cuda):
+    """Four host threads call the emitted entries at once, twenty rounds each (ctypes lets go of the interpreter lock
+    for the call): every thread has the reference's thread-local context over this machine, with its own stream
+    and arena, while the machine's per-device state (the memory pool, the SM count, the resident-grid memos) is
+    shared. Every result is still the oracle's."""
+    import threading
+
+    n = 1_000_003
+    cases = []
+    for t in range(4):
+        x_np, y_np, a = inputs.saxpy_case(n, seed=100 + t)
+        w = np.random.default_rng(200 + t).integers(0, 1 << 32, n, dtype=np.uint64).astype(np.uint32)
+        u = np.random.default_rng(300 + t).integers(0, 1 << 40, n, dtype=np.uint64)
+        cases.append(dict(x=_dev(x_np, cuda), y=_dev(y_np, cuda), a=float(a), w=_dev(w.view(np.int32), cuda),
+                          u=_dev(u.view(np.int64), cuda), out=torch.empty(n, dtype=torch.float32, device=cuda),
+                          wout=torch.empty(n, dtype=torch.int32, device=cuda),
+                          saxpy=restated.saxpy(float(a), x_np, y_np).view(np.uint32),
+                          scan=restated.scan_u32(w), usum=int(u.sum(dtype=np.uint64))))
+    torch.cuda.synchronize()
+    failures: list[str] = []
+
+    def work(t: int):
+        c = cases[t]
+        try:
+            for r in range(20):
+                emitted.cf_saxpy4(n, c["out"].data_ptr(), c["x"].data_ptr(), c["y"].data_ptr(), c["a"])
+                total = emitted.cf_wprefix(n, c["wout"].data_ptr(), c["w"].data_ptr())
+                usum = emitted.cf_usum(n, c["u"].data_ptr())
+                if total != c["scan"][1] or usum != c["usum"]:
+                    failures.append(f"thread {t} round {r}: totals {total} {usum}")
+        except Exception as e:  # noqa: BLE001 - reported below
+            failures.append(f"thread {t}: {e!r}")
+
+    threads = [threading.Thread(target=work, args=(t,)) for t in range(4)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join(timeout=300)
+    assert not any(th.is_alive() for th in threads)
+    assert not failures, failures[:4]
+    torch.cuda.synchronize()
+    for c in cases:
+        assert np.array_equal(_bits(c["out"]), c["saxpy"])
+        assert np.array_equal(c["wout"].cpu().numpy().view(np.uint32), c["scan"][0])
