@@ -520,3 +520,73 @@ def test_emitted_entries_from_several_host_threads_at_once(emitted, cuda):
     for c in cases:
         assert np.array_equal(_bits(c["out"]), c["saxpy"])
         assert np.array_equal(c["wout"].cpu().numpy().view(np.uint32), c["scan"][0])
+
+
+# ---- the enqueued entries inside a CUDA graph ----------------------------------------------------------------------
+# argv = repository root, library, inputs .npz, outputs .npz. A process of its own: a capture that failed would end in
+# the reference's trap (std::abort on the host), not in an exception.
+_IN_A_GRAPH = r"""
+import ctypes as C, sys
+import numpy as np, torch
+sys.path[:0] = [sys.argv[1]]
+import cairn_b200
+cairn_b200.lib()
+h = C.CDLL(sys.argv[2])
+z, p, f = C.c_size_t, C.c_void_p, C.c_float
+h.cq_saxpy4.restype, h.cq_saxpy4.argtypes = None, [p, z, p, p, p, f]
+h.cq_blur.restype, h.cq_blur.argtypes = None, [p, z, p, p]
+h.cq_gemm.restype, h.cq_gemm.argtypes = None, [p, z, z, z, z, p, z, p, z, p]
+d = dict(np.load(sys.argv[3]))
+dev = torch.device("cuda", 0)
+g = lambda v: torch.from_numpy(v).to(dev)
+x, y, a = g(d["x"]), g(d["y"]), float(d["a"][0])
+n = x.numel()
+m, nn, k = (int(v) for v in d["mnk"])
+ga, gb = g(d["ga"].view(np.int16)), g(d["gb"].view(np.int16))
+out4, blur = torch.empty_like(x), torch.empty_like(x)
+once, twice = torch.zeros(m * nn, device=dev), torch.zeros(m * nn, device=dev)
+s = torch.cuda.Stream(dev)
+torch.cuda.synchronize()
+def enqueue(c):
+    h.cq_saxpy4(s.cuda_stream, n, out4.data_ptr(), x.data_ptr(), y.data_ptr(), a)
+    h.cq_blur(s.cuda_stream, n, blur.data_ptr(), x.data_ptr())
+    h.cq_gemm(s.cuda_stream, m, nn, k, m * nn, c.data_ptr(), m * k, ga.data_ptr(), k * nn, gb.data_ptr())
+with torch.cuda.stream(s):
+    enqueue(once)  # outside a capture first: the machine sizes its grids and the multiply configures its kernel
+s.synchronize()
+graph = torch.cuda.CUDAGraph()
+with torch.cuda.graph(graph, stream=s):
+    enqueue(twice)
+out4.zero_(); blur.zero_(); twice.zero_()
+torch.cuda.synchronize()
+graph.replay()
+graph.replay()  # C += A B twice: every element is twice the single product, exactly
+torch.cuda.synchronize()
+np.savez(sys.argv[4], saxpy4=out4.cpu().numpy(), blur=blur.cpu().numpy(), once=once.cpu().numpy(),
+         twice=twice.cpu().numpy())
+"""
+
+
+def test_the_enqueued_entries_run_inside_a_cuda_graph(emitted, cuda, tmp_path):
+    """cq_saxpy4 (a vector region), cq_blur (a staged region) and cq_gemm (`mma_unordered` over the B200 multiply)
+    captured in one CUDA graph on the caller's stream after one call outside it, as the header says an enqueued
+    entry may be (it makes no stream, event or allocation): the graph replays to the oracle's saxpy and blur bits,
+    and two replays of C += A B give exactly twice one call's product."""
+    n = 1_000_003
+    x, y, a = inputs.saxpy_case(n, seed=77)
+    m, nn, k = 512, 768, 256
+    _, ga, gb = inputs.mma_case("bf16", m, nn, k, seed=8)
+    src, dst = tmp_path / "in.npz", tmp_path / "out.npz"
+    np.savez(src, x=x, y=y, a=np.asarray([a], np.float32), ga=ga, gb=gb, mnk=np.asarray([m, nn, k]))
+    done = subprocess.run([sys.executable, "-c", _IN_A_GRAPH, str(ROOT), str(LIB), str(src), str(dst)],
+                          capture_output=True, text=True, timeout=600)
+    assert done.returncode == 0, (done.returncode, done.stderr[-3000:])
+    got = np.load(dst)
+    assert np.array_equal(got["saxpy4"].view(np.uint32), restated.saxpy(float(a), x, y).view(np.uint32))
+    assert np.array_equal(got["blur"].view(np.uint32), _blur(x).view(np.uint32))
+    assert np.array_equal(got["twice"], got["once"] * np.float32(2))
+    want = restated.mma("bf16", np.zeros(m * nn, np.float32), ga, gb, m, nn, k)
+    av = np.abs(inputs.decode("bf16", ga).reshape(m, k))
+    bv = np.abs(inputs.decode("bf16", gb).reshape(k, nn))
+    tol = 2 * (k + 1) * 2.0**-22 * (av @ bv)
+    assert (np.abs(got["once"].reshape(m, nn) - want.reshape(m, nn)) <= tol).all()
