@@ -20,11 +20,16 @@
 //   chunks, and the fewer than W indices past the last whole chunk run by the last block, one thread each. For f32
 //   and W = 4 each access is 16 bytes; this shape ran 7.1 TB/s for saxpy, where a grid-stride loop over 65,535
 //   blocks ran 6.9 and a persistent grid 6.3.
-// * `plan stage R`: one tile of shared memory per block, each block taking a run of STAGE_TILES = 64 consecutive
-//   tiles (or per_lane, if larger), between the two barriers run_staged's rule asks for. Consecutive tiles share
-//   their halos in cache; 2.49 TB/s for the blur against 1.69 with one tile per block. Two tiles per block, loading
-//   the next while the lanes read the current one, measured slower (2.31): the load body's loads must land before
-//   its stores into the tile, so nothing overlapped, and the second tile halved the blocks resident per SM.
+// * `plan stage R`: one tile of shared memory per block, STAGE_WIDTHS = 4 block widths wide (plus the 2R halo), each
+//   thread running the body at four indices of it, and each block taking a run of consecutive tiles (STAGE_TILES
+//   block widths' worth, or per_lane tiles if larger), between the two barriers run_staged's rule asks for. The
+//   emitted load and lane bodies take the tile's width as an argument (compiler/plans/staging.py:85-120: the load
+//   loops over it, the arrays' offsets and bytes follow it), so a tile may hold several block widths. Measured on a
+//   B200 for the blur (n = 2^30): tiles of 1, 2, 3, 4, 5, 6 and 8 block widths ran 2.29, 2.09, 2.07, 3.10, 2.32, 2.34
+//   and 2.40 TB/s (the reference's machine, one width: 2.17); with four, the load body's four loads per thread are
+//   in flight together. Consecutive tiles share their halos in cache (a run of tiles per block ran 2.49 TB/s
+//   against 1.69 with one tile per block, at one width). Two one-width tiles per block, loading the next while the
+//   lanes read the current one, measured slower (2.31): the loads must land before their stores into the tile.
 //
 // Build a program with this directory ahead of the reference's runtime directory on the include path.
 #pragma once
@@ -97,7 +102,8 @@ inline std::size_t resident_blocks(std::atomic<unsigned long long>& last, K kern
 }
 
 constexpr std::size_t LANE_INDICES = 64;  // indices per thread a plain region's grid aims at
-constexpr std::size_t STAGE_TILES = 64;   // consecutive tiles per block of a staged region
+constexpr std::size_t STAGE_TILES = 64;   // block widths of consecutive tiles per block of a staged region
+constexpr std::size_t STAGE_WIDTHS = 4;   // block widths per staged tile
 constexpr std::size_t GRID_LIMIT = 0x7fffffff;
 
 // The grid for `units` units of work (indices, chunks or tiles), `per` per thread or block as the caller counts
@@ -174,21 +180,26 @@ inline void start_chunks(std::size_t n, F scalar, G chunk, cudaStream_t s, unsig
   check(cudaGetLastError());
 }
 
-// `plan f { stage R; }`: a tile covers blockDim.x indices from `base`; `load(base, w, t, b, tile)` fills the tile
-// with the staged arrays' elements from base - R to base + b + R that lie inside them, and `body(i, base, w, tile)`
-// runs index i reading them there (runtime/cairn_exec.hpp's run_staged). Block b takes tiles b * span to
-// b * span + span - 1. Every thread of a block reaches every barrier: the loop bounds depend on the block alone.
-template<std::size_t R, class L, class F> __global__ void region_staged(std::size_t n, std::size_t span, L load, F body) {
+// `plan f { stage R; }`: a tile covers K block widths of indices from `base` (STAGE_WIDTHS, or one where the wider
+// tile would take more than 48 KB of shared memory); `load(base, w, t, b,
+// tile)` fills the tile (w = K b + 2R) with the staged arrays' elements from base - R to base + K b + R that lie
+// inside them, and `body(i, base, w, tile)` runs each index i of the tile reading them there, thread t at base + t,
+// base + b + t, ... (runtime/cairn_exec.hpp's run_staged). Block b takes tiles b * span to b * span + span - 1.
+// Every thread of a block reaches every barrier: the loop bounds depend on the block alone.
+template<std::size_t R, std::size_t K, class L, class F>
+__global__ void region_staged(std::size_t n, std::size_t span, L load, F body) {
   extern __shared__ __align__(128) unsigned char tile_smem[];
-  const std::size_t b = blockDim.x, w = b + 2 * R, t = threadIdx.x, tiles = (n + b - 1) / b;
+  const std::size_t b = blockDim.x, w = K * b + 2 * R, t = threadIdx.x, tiles = (n + K * b - 1) / (K * b);
   const std::size_t first = std::size_t(blockIdx.x) * span, last = first + span < tiles ? first + span : tiles;
 #pragma unroll 1
   for(std::size_t tile = first; tile < last; ++tile) {
-    const std::size_t base = tile * b;
+    const std::size_t base = tile * K * b;
     __syncthreads();  // the lanes of the previous tile are done with it
     load(base, w, t, b, tile_smem);
     __syncthreads();
-    if(base + t < n) body(base + t, base, w, tile_smem);
+#pragma unroll
+    for(std::size_t k = 0; k < K; ++k)
+      if(base + k * b + t < n) body(base + k * b + t, base, w, tile_smem);
   }
 }
 
@@ -198,22 +209,32 @@ inline void start_staged(std::size_t n, L load, F body, S bytes, cudaStream_t s,
   static_assert(std::is_trivially_copyable_v<L> && std::is_trivially_copyable_v<F>, "lanes cross as arguments");
   (void)U;  // a tile's barriers leave nothing to unroll
   if(!n) return;
-  static const unsigned most = widest_block(region_staged<R, L, F>);
-  static std::atomic<unsigned long long> fit{0};
+  static const unsigned most = [] {  // the widest block both tile widths' kernels launch with
+    const unsigned one = widest_block(region_staged<R, 1, L, F>);
+    const unsigned wide = widest_block(region_staged<R, STAGE_WIDTHS, L, F>);
+    return one < wide ? one : wide;
+  }();
   if(block > most) block = most;
   if(block < WARP) block = WARP;
-  const std::size_t shared = bytes(std::size_t(block) + 2 * R);
-  if(shared > 48 * 1024)
-    check(cudaFuncSetAttribute(region_staged<R, L, F>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(shared)));
-  const std::size_t tiles = (n + block - 1) / block;
-  std::size_t span = per_lane > STAGE_TILES ? per_lane : STAGE_TILES;
-  while((tiles + span - 1) / span > GRID_LIMIT) span *= 2;
-  // a grid of at least the resident blocks (when there are tiles for them), each block `span` tiles or fewer
-  const std::size_t resident = resident_blocks(fit, region_staged<R, L, F>, block, shared);
-  const unsigned grid = region_grid(tiles, 1, span, resident);
-  const std::size_t each = (tiles + grid - 1) / grid;
-  region_staged<R><<<grid, block, shared, s>>>(n, each, load, body);
-  check(cudaGetLastError());
+  auto launch = [&](auto kernel, std::size_t k, std::atomic<unsigned long long>& fit) {
+    const std::size_t shared = bytes(k * block + 2 * R);
+    if(shared > 48 * 1024)
+      check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(shared)));
+    const std::size_t tiles = (n + k * block - 1) / (k * block);
+    std::size_t span = per_lane > STAGE_TILES / k ? per_lane : STAGE_TILES / k;  // STAGE_TILES widths per block
+    while((tiles + span - 1) / span > GRID_LIMIT) span *= 2;
+    // a grid of at least the resident blocks (when there are tiles for them), each block `span` tiles or fewer
+    const std::size_t resident = resident_blocks(fit, kernel, block, shared);
+    const unsigned grid = region_grid(tiles, 1, span, resident);
+    const std::size_t each = (tiles + grid - 1) / grid;
+    kernel<<<grid, block, shared, s>>>(n, each, load, body);
+    check(cudaGetLastError());
+  };
+  static std::atomic<unsigned long long> fit_wide{0}, fit_one{0};
+  if(bytes(STAGE_WIDTHS * block + 2 * R) <= 48 * 1024)
+    launch(region_staged<R, STAGE_WIDTHS, L, F>, STAGE_WIDTHS, fit_wide);
+  else
+    launch(region_staged<R, 1, L, F>, 1, fit_one);
 }
 
 }  // namespace b200
