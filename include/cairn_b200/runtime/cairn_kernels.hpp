@@ -221,7 +221,9 @@ inline void start_staged(std::size_t n, L load, F body, S bytes, cudaStream_t s,
     if(shared > 48 * 1024)
       check(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(shared)));
     const std::size_t tiles = (n + k * block - 1) / (k * block);
-    std::size_t span = per_lane > STAGE_TILES / k ? per_lane : STAGE_TILES / k;  // STAGE_TILES widths per block
+    // a block's run: per_lane block widths (the plan's tiles per block) or STAGE_TILES widths, whichever is more
+    const std::size_t asked = (per_lane + k - 1) / k;
+    std::size_t span = asked > STAGE_TILES / k ? asked : STAGE_TILES / k;
     while((tiles + span - 1) / span > GRID_LIMIT) span *= 2;
     // a grid of at least the resident blocks (when there are tiles for them), each block `span` tiles or fewer
     const std::size_t resident = resident_blocks(fit, kernel, block, shared);
