@@ -20,14 +20,17 @@
 //   chunks, and the fewer than W indices past the last whole chunk run by the last block, one thread each. For f32
 //   and W = 4 each access is 16 bytes; this shape ran 7.1 TB/s for saxpy, where a grid-stride loop over 65,535
 //   blocks ran 6.9 and a persistent grid 6.3.
-// * `plan stage R`: one tile of shared memory per block, STAGE_WIDTHS = 4 block widths wide (plus the 2R halo), each
-//   thread running the body at four indices of it, and each block taking a run of consecutive tiles (STAGE_TILES
-//   block widths' worth, or per_lane tiles if larger), between the two barriers run_staged's rule asks for. The
+// * `plan stage R`: one tile of shared memory per block, several block widths wide (plus the 2R halo), each thread
+//   running the body at as many indices of it, and each block taking a run of consecutive tiles (STAGE_TILES block
+//   widths' worth, or the plan's per_lane widths if more), between the two barriers run_staged's rule asks for. The
 //   emitted load and lane bodies take the tile's width as an argument (compiler/plans/staging.py:85-120: the load
-//   loops over it, the arrays' offsets and bytes follow it), so a tile may hold several block widths. Measured on a
-//   B200 for the blur (n = 2^30): tiles of 1, 2, 3, 4, 5, 6 and 8 block widths ran 2.29, 2.09, 2.07, 3.10, 2.32, 2.34
-//   and 2.40 TB/s (the reference's machine, one width: 2.17); with four, the load body's four loads per thread are
-//   in flight together. Consecutive tiles share their halos in cache (a run of tiles per block ran 2.49 TB/s
+//   loops over it, the arrays' offsets and bytes follow it), so a tile may hold several block widths. For blocks of
+//   128 or 256 threads a tile holds STAGE_WIDE = 2048 indices and the kernel is compiled for that block width, so the
+//   load loop's trip count is known and every one of a thread's loads is in flight at once; other blocks take four
+//   widths with the width known only at launch. Measured on a B200 for the blur (n = 2^30, blocks of 128): the
+//   width known at launch, tiles of 1, 2, 3, 4, 5, 6 and 8 block widths ran 2.29, 2.09, 2.07, 3.10, 2.32, 2.34 and
+//   2.40 TB/s; known where compiled, 4, 8, 16, 32 and 64 widths 2.98, 4.46, 4.93, 4.21 and 2.25 (the reference's
+//   machine, one width: 2.17). Consecutive tiles share their halos in cache (a run of tiles per block ran 2.49 TB/s
 //   against 1.69 with one tile per block, at one width). Two one-width tiles per block, loading the next while the
 //   lanes read the current one, measured slower (2.31): the loads must land before their stores into the tile.
 //
@@ -103,7 +106,8 @@ inline std::size_t resident_blocks(std::atomic<unsigned long long>& last, K kern
 
 constexpr std::size_t LANE_INDICES = 64;  // indices per thread a plain region's grid aims at
 constexpr std::size_t STAGE_TILES = 64;   // block widths of consecutive tiles per block of a staged region
-constexpr std::size_t STAGE_WIDTHS = 4;   // block widths per staged tile
+constexpr std::size_t STAGE_WIDTHS = 4;   // block widths per staged tile, for a block width known only at launch
+constexpr std::size_t STAGE_WIDE = 2048;  // indices per staged tile for blocks of 128 or 256 threads
 constexpr std::size_t GRID_LIMIT = 0x7fffffff;
 
 // The grid for `units` units of work (indices, chunks or tiles), `per` per thread or block as the caller counts
@@ -180,16 +184,19 @@ inline void start_chunks(std::size_t n, F scalar, G chunk, cudaStream_t s, unsig
   check(cudaGetLastError());
 }
 
-// `plan f { stage R; }`: a tile covers K block widths of indices from `base` (STAGE_WIDTHS, or one where the wider
-// tile would take more than 48 KB of shared memory); `load(base, w, t, b,
+// `plan f { stage R; }`: a tile covers K block widths of indices from `base` (STAGE_WIDE / B for blocks of B = 128 or
+// 256 threads, STAGE_WIDTHS for other blocks, or one where the wider tile would take more than 48 KB of shared
+// memory); `load(base, w, t, b,
 // tile)` fills the tile (w = K b + 2R) with the staged arrays' elements from base - R to base + K b + R that lie
 // inside them, and `body(i, base, w, tile)` runs each index i of the tile reading them there, thread t at base + t,
 // base + b + t, ... (runtime/cairn_exec.hpp's run_staged). Block b takes tiles b * span to b * span + span - 1.
 // Every thread of a block reaches every barrier: the loop bounds depend on the block alone.
-template<std::size_t R, std::size_t K, class L, class F>
+template<std::size_t R, std::size_t K, unsigned B, class L, class F>
 __global__ void region_staged(std::size_t n, std::size_t span, L load, F body) {
   extern __shared__ __align__(128) unsigned char tile_smem[];
-  const std::size_t b = blockDim.x, w = K * b + 2 * R, t = threadIdx.x, tiles = (n + K * b - 1) / (K * b);
+  // B: the block width when it is known where the kernel is compiled (the launcher picks this kernel only for
+  // blocks of B threads), so that the load body's loop over the tile has a known trip count; 0: blockDim.x
+  const std::size_t b = B ? B : blockDim.x, w = K * b + 2 * R, t = threadIdx.x, tiles = (n + K * b - 1) / (K * b);
   const std::size_t first = std::size_t(blockIdx.x) * span, last = first + span < tiles ? first + span : tiles;
 #pragma unroll 1
   for(std::size_t tile = first; tile < last; ++tile) {
@@ -210,8 +217,8 @@ inline void start_staged(std::size_t n, L load, F body, S bytes, cudaStream_t s,
   (void)U;  // a tile's barriers leave nothing to unroll
   if(!n) return;
   static const unsigned most = [] {  // the widest block both tile widths' kernels launch with
-    const unsigned one = widest_block(region_staged<R, 1, L, F>);
-    const unsigned wide = widest_block(region_staged<R, STAGE_WIDTHS, L, F>);
+    const unsigned one = widest_block(region_staged<R, 1, 0, L, F>);
+    const unsigned wide = widest_block(region_staged<R, STAGE_WIDTHS, 0, L, F>);
     return one < wide ? one : wide;
   }();
   if(block > most) block = most;
@@ -232,11 +239,16 @@ inline void start_staged(std::size_t n, L load, F body, S bytes, cudaStream_t s,
     kernel<<<grid, block, shared, s>>>(n, each, load, body);
     check(cudaGetLastError());
   };
-  static std::atomic<unsigned long long> fit_wide{0}, fit_one{0};
-  if(bytes(STAGE_WIDTHS * block + 2 * R) <= 48 * 1024)
-    launch(region_staged<R, STAGE_WIDTHS, L, F>, STAGE_WIDTHS, fit_wide);
+  static std::atomic<unsigned long long> fit_128{0}, fit_256{0}, fit_wide{0}, fit_one{0};
+  constexpr std::size_t LIMIT = 48 * 1024;
+  if(block == 128 && bytes(STAGE_WIDE + 2 * R) <= LIMIT)
+    launch(region_staged<R, STAGE_WIDE / 128, 128, L, F>, STAGE_WIDE / 128, fit_128);
+  else if(block == 256 && bytes(STAGE_WIDE + 2 * R) <= LIMIT)
+    launch(region_staged<R, STAGE_WIDE / 256, 256, L, F>, STAGE_WIDE / 256, fit_256);
+  else if(bytes(STAGE_WIDTHS * block + 2 * R) <= LIMIT)
+    launch(region_staged<R, STAGE_WIDTHS, 0, L, F>, STAGE_WIDTHS, fit_wide);
   else
-    launch(region_staged<R, 1, L, F>, 1, fit_one);
+    launch(region_staged<R, 1, 0, L, F>, 1, fit_one);
 }
 
 }  // namespace b200
