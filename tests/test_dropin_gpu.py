@@ -40,7 +40,7 @@ ENTRIES = {
     "cf_saxpy4": (None, [z, p, p, p, f32]), "cq_saxpy4": (None, [p, z, p, p, p, f32]),
     "cf_scaled": (None, [z, p, f32]), "cq_scaled": (None, [p, z, p, f32]),
     "cf_blend": (None, [z, p, p, f32, f32]),
-    "cf_blur": (None, [z, p, p]), "cq_blur": (None, [p, z, p, p]),
+    "cf_blur": (None, [z, p, p]), "cq_blur": (None, [p, z, p, p]), "cf_mix": (None, [z, p, p, p]),
     "cf_dsum": (f32, [z, p]), "cf_usum": (u64, [z, p]), "cf_vmax": (i32, [z, p]), "cf_usum_into": (None, [z, p, p]),
     "cf_prefix": (u64, [z, p, p]), "cf_wprefix": (u32, [z, p, p]), "cf_runmax": (i32, [z, p, p]),
     "cf_wscan": (None, [z, p, p]), "cf_positives": (z, [z, p, p]),
@@ -170,6 +170,22 @@ def test_emitted_staged_region(emitted, cuda, n):
         emitted.cq_blur(s.cuda_stream, n, out.data_ptr(), x.data_ptr())
     s.synchronize()
     assert np.array_equal(_bits(out), _blur(x_np).view(np.uint32))
+
+
+@pytest.mark.parametrize("n", [1, 2, 3, 255, 256, 257, 2047, 2048, 2049, 2051, 100_003, 4_194_305])
+def test_emitted_staged_region_of_two_arrays_at_the_default_block(emitted, cuda, n):
+    """`plan mix { stage 1; }`: an f32 and an f64 array staged in one tile (the f64 one placed after the f32 one's
+    bytes, both sized by the tile's width), at the plan's default block of 256 threads, whose tiles hold 2048
+    indices: out = (f64(x[i-1]) + y[i+1]) - y[i-1] * 0.5 inside, y[i] at the ends, bit for bit."""
+    rng = np.random.default_rng(n + 11)
+    x = rng.uniform(-1, 1, n).astype(np.float32)
+    y = rng.uniform(-1, 1, n)
+    xd, yd, out = _dev(x, cuda), _dev(y, cuda), torch.empty(n, dtype=torch.float64, device=cuda)
+    emitted.cf_mix(n, out.data_ptr(), xd.data_ptr(), yd.data_ptr())
+    want = y.copy()
+    if n >= 3:
+        want[1:-1] = (x[:-2].astype(np.float64) + y[2:]) - y[:-2] * 0.5
+    assert np.array_equal(out.cpu().numpy().view(np.uint64), want.view(np.uint64))
 
 
 def test_a_bound_stream_orders_the_synchronous_entries(emitted, cuda):
