@@ -186,11 +186,11 @@ inline void start_chunks(std::size_t n, F scalar, G chunk, cudaStream_t s, unsig
 
 // `plan f { stage R; }`: a tile covers K block widths of indices from `base` (STAGE_WIDE / B for blocks of B = 128 or
 // 256 threads, STAGE_WIDTHS for other blocks, or one where the wider tile would take more than 48 KB of shared
-// memory); `load(base, w, t, b,
-// tile)` fills the tile (w = K b + 2R) with the staged arrays' elements from base - R to base + K b + R that lie
-// inside them, and `body(i, base, w, tile)` runs each index i of the tile reading them there, thread t at base + t,
-// base + b + t, ... (runtime/cairn_exec.hpp's run_staged). Block b takes tiles b * span to b * span + span - 1.
-// Every thread of a block reaches every barrier: the loop bounds depend on the block alone.
+// memory); `load(base, w, t, b, tile)` fills the tile (w = K b + 2R) with the staged arrays' elements from base - R
+// to base + K b + R that lie inside them, and `body(i, base, w, tile)` runs each index i of the tile reading them
+// there, thread t at base + t, base + b + t, ... (runtime/cairn_exec.hpp's run_staged). Block b takes tiles
+// b * span to b * span + span - 1. Every thread of a block reaches every barrier: the loop bounds depend on the
+// block alone.
 template<std::size_t R, std::size_t K, unsigned B, class L, class F>
 __global__ void region_staged(std::size_t n, std::size_t span, L load, F body) {
   extern __shared__ __align__(128) unsigned char tile_smem[];
