@@ -29,8 +29,8 @@
 //   load loop's trip count is known and every one of a thread's loads is in flight at once; other blocks take four
 //   widths with the width known only at launch. Measured on a B200 for the blur (n = 2^30, blocks of 128): the
 //   width known at launch, tiles of 1, 2, 3, 4, 5, 6 and 8 block widths ran 2.29, 2.09, 2.07, 3.10, 2.32, 2.34 and
-//   2.40 TB/s; known where compiled, 4, 8, 16, 32 and 64 widths 2.98, 4.46, 4.93, 4.21 and 2.25 (the reference's
-//   machine, one width: 2.17). Consecutive tiles share their halos in cache (a run of tiles per block ran 2.49 TB/s
+//   2.40 TB/s; known where compiled, 4, 8, 16, 32 and 64 widths 2.98, 4.46, 4.93, 4.21 and 2.25, and 5.15-5.48 with
+//   16 widths held to 32 registers (the reference's machine, one width: 2.17). Consecutive tiles share their halos in cache (a run of tiles per block ran 2.49 TB/s
 //   against 1.69 with one tile per block, at one width). Two one-width tiles per block, loading the next while the
 //   lanes read the current one, measured slower (2.31): the loads must land before their stores into the tile.
 //
@@ -192,9 +192,9 @@ inline void start_chunks(std::size_t n, F scalar, G chunk, cudaStream_t s, unsig
 // b * span to b * span + span - 1. Every thread of a block reaches every barrier: the loop bounds depend on the
 // block alone.
 template<std::size_t R, std::size_t K, unsigned B, class L, class F>
-__global__ void region_staged(std::size_t n, std::size_t span, L load, F body) {
+__device__ __forceinline__ void staged_tiles(std::size_t n, std::size_t span, L& load, F& body) {
   extern __shared__ __align__(128) unsigned char tile_smem[];
-  // B: the block width when it is known where the kernel is compiled (the launcher picks this kernel only for
+  // B: the block width when it is known where the kernel is compiled (the launcher picks such a kernel only for
   // blocks of B threads), so that the load body's loop over the tile has a known trip count; 0: blockDim.x
   const std::size_t b = B ? B : blockDim.x, w = K * b + 2 * R, t = threadIdx.x, tiles = (n + K * b - 1) / (K * b);
   const std::size_t first = std::size_t(blockIdx.x) * span, last = first + span < tiles ? first + span : tiles;
@@ -209,6 +209,17 @@ __global__ void region_staged(std::size_t n, std::size_t span, L load, F body) {
       if(base + k * b + t < n) body(base + k * b + t, base, w, tile_smem);
   }
 }
+// The width known at launch.
+template<std::size_t R, std::size_t K, class L, class F>
+__global__ void region_staged(std::size_t n, std::size_t span, L load, F body) {
+  staged_tiles<R, K, 0>(n, span, load, body);
+}
+// The width known where compiled, held to the registers that let an SM hold 2048 / B blocks of it (measured on a
+// B200 for the blur at B = 128: 5.15 TB/s against 4.93 with the compiler's 39 registers, 12 blocks per SM).
+template<std::size_t R, std::size_t K, unsigned B, class L, class F>
+__global__ void __launch_bounds__(B, 2048 / B) region_staged_fixed(std::size_t n, std::size_t span, L load, F body) {
+  staged_tiles<R, K, B>(n, span, load, body);
+}
 
 template<std::size_t R, unsigned U, class L, class F, class S>
 inline void start_staged(std::size_t n, L load, F body, S bytes, cudaStream_t s, unsigned block,
@@ -217,8 +228,8 @@ inline void start_staged(std::size_t n, L load, F body, S bytes, cudaStream_t s,
   (void)U;  // a tile's barriers leave nothing to unroll
   if(!n) return;
   static const unsigned most = [] {  // the widest block both tile widths' kernels launch with
-    const unsigned one = widest_block(region_staged<R, 1, 0, L, F>);
-    const unsigned wide = widest_block(region_staged<R, STAGE_WIDTHS, 0, L, F>);
+    const unsigned one = widest_block(region_staged<R, 1, L, F>);
+    const unsigned wide = widest_block(region_staged<R, STAGE_WIDTHS, L, F>);
     return one < wide ? one : wide;
   }();
   if(block > most) block = most;
@@ -242,13 +253,13 @@ inline void start_staged(std::size_t n, L load, F body, S bytes, cudaStream_t s,
   static std::atomic<unsigned long long> fit_128{0}, fit_256{0}, fit_wide{0}, fit_one{0};
   constexpr std::size_t LIMIT = 48 * 1024;
   if(block == 128 && bytes(STAGE_WIDE + 2 * R) <= LIMIT)
-    launch(region_staged<R, STAGE_WIDE / 128, 128, L, F>, STAGE_WIDE / 128, fit_128);
+    launch(region_staged_fixed<R, STAGE_WIDE / 128, 128, L, F>, STAGE_WIDE / 128, fit_128);
   else if(block == 256 && bytes(STAGE_WIDE + 2 * R) <= LIMIT)
-    launch(region_staged<R, STAGE_WIDE / 256, 256, L, F>, STAGE_WIDE / 256, fit_256);
+    launch(region_staged_fixed<R, STAGE_WIDE / 256, 256, L, F>, STAGE_WIDE / 256, fit_256);
   else if(bytes(STAGE_WIDTHS * block + 2 * R) <= LIMIT)
-    launch(region_staged<R, STAGE_WIDTHS, 0, L, F>, STAGE_WIDTHS, fit_wide);
+    launch(region_staged<R, STAGE_WIDTHS, L, F>, STAGE_WIDTHS, fit_wide);
   else
-    launch(region_staged<R, 1, 0, L, F>, 1, fit_one);
+    launch(region_staged<R, 1, L, F>, 1, fit_one);
 }
 
 }  // namespace b200
