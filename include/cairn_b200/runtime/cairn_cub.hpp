@@ -506,7 +506,19 @@ __global__ void __launch_bounds__(SCAN_BLOCK, SCAN_BLOCKS_PER_SM)
   }
   workers_sync();
 
-  // write: this warp's rows again, each element with its segment's prefix
+  // write: this warp's rows again, each element with its segment's prefix. A whole tile of an inclusive scan takes a
+  // loop with no bounds test and 32-bit offsets (a tile holds at most 16,384 elements), which unrolls.
+  if constexpr(!Exclusive) {
+    if(full) {
+#pragma unroll 8
+      for(unsigned r = 0; r < ROWS; ++r) {
+        const unsigned e = (warp * ROWS + r) * 32 + lane, s = e / S;
+        const T v = vals[e + s];
+        out[tile0 + e] = seg_ok[s] ? fold(seg[s], v) : v;
+      }
+      return;
+    }
+  }
   for(unsigned r = 0; r < ROWS; ++r) {
     const std::size_t e = (std::size_t(warp) * ROWS + r) * 32 + lane;
     if(e >= valid) break;
